@@ -17,7 +17,8 @@
 // Usage:
 //   ref_harness --model <hf_repo_root> --prompt <ids.bin int64> --decode <n>
 //               [--out <file>] [--kvgb <n>] [--nokv] [--topk K --temp T --seed S]
-//               [--mask <ids.bin int64>] [--threads N]
+//               [--mask <ids.bin int64>] [--threads N] [--warmup W]
+// --warmup W leaves the first W decode tokens out of the timed sum.
 #include "Model.h"
 #include "ConfigManager.h"
 #include <torch/torch.h>
@@ -72,7 +73,7 @@ int64_t sample_like_reference(torch::Tensor &last, bool greedy, int topk, float 
 int main(int argc, char **argv)
 {
     std::string model, prompt_path, out_path, mask_path;
-    int n_decode = 8, kvgb = 2, topk = 0, threads = 0;
+    int n_decode = 8, kvgb = 2, topk = 0, threads = 0, warmup = 0;
     float temp = 0.6f;
     int64_t seed = 0;
     bool kv = true;
@@ -96,6 +97,7 @@ int main(int argc, char **argv)
         else if (a == "--seed") seed = std::stoll(next());
         else if (a == "--mask") mask_path = next();
         else if (a == "--threads") threads = std::stoi(next());
+        else if (a == "--warmup") warmup = std::stoi(next());
         else throw std::runtime_error("unknown argument " + a);
     }
     if (threads > 0)
@@ -157,9 +159,9 @@ int main(int argc, char **argv)
         int64_t id = sample_like_reference(last, greedy, ConfigManager::TopK, ConfigManager::Temp, masked);
         auto t1 = std::chrono::steady_clock::now();
         double dt = std::chrono::duration<double>(t1 - t0).count();
-        if (generated > 0)
+        if (generated > warmup)
             token_times += dt;
-        else
+        else if (generated == 0)
             first_time = dt;
         generated++;
         ids.push_back(id);
@@ -179,11 +181,12 @@ int main(int argc, char **argv)
     if (out)
         std::fclose(out);
 
-    double tps = (generated <= 1 ? 0.0 : (generated - 1) / (token_times == 0.0 ? 1.0 : token_times));
+    const int timed = generated - 1 - warmup;
+    double tps = (timed <= 0 ? 0.0 : timed / (token_times == 0.0 ? 1.0 : token_times));
     std::printf("{\"generated\": %d, \"error\": %d, \"first_token_s\": %.6f, \"decode_s\": %.6f, "
-                "\"tokens_per_second\": %.6f, \"load_s\": %.3f, \"threads\": %d, \"prompt_len\": %zu}\n",
+                "\"tokens_per_second\": %.6f, \"load_s\": %.3f, \"threads\": %d, \"prompt_len\": %zu, \"timed_tokens\": %d}\n",
                 generated, error, first_time, token_times, tps,
                 std::chrono::duration<double>(t_load1 - t_load0).count(),
-                (int)torch::get_num_threads(), prompt.size());
+                (int)torch::get_num_threads(), prompt.size(), timed > 0 ? timed : 0);
     return 0;
 }

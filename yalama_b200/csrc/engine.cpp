@@ -1,0 +1,1567 @@
+// yalama_b200 engine: the host side of the batch-1 decode path, behind the C
+// ABI of include/yalama_b200.h.
+//
+// It owns what ModelBase owns in the reference (src/models/ModelBase.cpp): the
+// weights, the fixed-size KV cache, the RoPE tables and the
+// _LastKVCacheTokenIndex state machine, and it drives the sm_100a kernels of
+// this directory instead of LibTorch ops. Decode steps are captured once as a
+// CUDA graph (kernels chained with programmatic dependent launch); per-step
+// values (token, KV slot, RoPE position, sampling state) live in a small
+// device-resident StepState so the same graph serves every step. Tensor
+// parallelism (Megatron-style: column-split QKV / gate-up, row-split O / down,
+// KV heads and vocabulary sharded) adds NCCL all-reduces after O and down and an
+// all-gather of the logits.
+#include "../../include/yalama_b200.h"
+#include "json_lite.h"
+#include "ylm_kernels.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <dirent.h>
+#include <fcntl.h>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+#include <vector>
+
+using namespace ylm;
+
+// ------------------------------------------------------------------ errors
+namespace {
+thread_local std::string g_last_error;
+
+struct YlmError : std::runtime_error
+{
+    int status;
+    YlmError(int s, const std::string &m) : std::runtime_error(m), status(s) {}
+};
+
+[[noreturn]] void fail(int status, const char *fmt, ...)
+{
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    throw YlmError(status, buf);
+}
+
+#define CK(call)                                                                                                      \
+    do                                                                                                                \
+    {                                                                                                                 \
+        cudaError_t e_ = (call);                                                                                      \
+        if (e_ != cudaSuccess)                                                                                        \
+            fail(YLM_CUDA_ERROR, "%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_));                  \
+    } while (0)
+
+#define NK(call)                                                                                                      \
+    do                                                                                                                \
+    {                                                                                                                 \
+        ncclResult_t r_ = (call);                                                                                     \
+        if (r_ != ncclSuccess)                                                                                        \
+            fail(YLM_COMM_ERROR, "%s:%d %s: %s", __FILE__, __LINE__, #call, ncclGetErrorString(r_));                  \
+    } while (0)
+
+template <typename F> int guarded(F &&f)
+{
+    try
+    {
+        g_last_error.clear();
+        return f();
+    }
+    catch (const YlmError &e)
+    {
+        g_last_error = e.what();
+        return e.status;
+    }
+    catch (const std::exception &e)
+    {
+        g_last_error = e.what();
+        return YLM_LOAD_ERROR;
+    }
+}
+
+std::string read_file(const std::string &p)
+{
+    std::ifstream f(p, std::ios::binary);
+    if (!f)
+        fail(YLM_LOAD_ERROR, "cannot open %s", p.c_str());
+    std::stringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+// FNV-1a 64 of a tensor name and the SplitMix64 finaliser: the stream key of
+// the counter-based initialiser (yalama_b200/synth.py, init.cu).
+uint64_t fnv1a64(const std::string &s)
+{
+    uint64_t h = 0xCBF29CE484222325ull;
+    for (unsigned char c : s)
+    {
+        h ^= c;
+        h *= 0x100000001B3ull;
+    }
+    return h;
+}
+uint64_t mix64(uint64_t z)
+{
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// ------------------------------------------------------------------ safetensors
+struct StTensor
+{
+    std::string dtype; // F16 / BF16 / F32
+    std::vector<int64_t> shape;
+    const uint8_t *data = nullptr;
+    size_t bytes = 0;
+};
+
+struct StFile
+{
+    int fd = -1;
+    void *map = nullptr;
+    size_t size = 0;
+    ~StFile()
+    {
+        if (map && map != MAP_FAILED)
+            munmap(map, size);
+        if (fd >= 0)
+            close(fd);
+    }
+};
+
+// mmap every *.safetensors shard of a snapshot folder and index its tensors
+// (ModelBase.cpp:42-85 and include/safetensors.h:37-111).
+struct Snapshot
+{
+    std::vector<std::unique_ptr<StFile>> files;
+    std::map<std::string, StTensor> tensors;
+
+    void open_dir(const std::string &dir)
+    {
+        DIR *d = opendir(dir.c_str());
+        if (!d)
+            fail(YLM_LOAD_ERROR, "Invalid model folder: %s", dir.c_str());
+        std::vector<std::string> names;
+        while (dirent *e = readdir(d))
+        {
+            std::string n = e->d_name;
+            if (n.size() > 12 && n.substr(n.size() - 12) == ".safetensors")
+                names.push_back(dir + "/" + n);
+        }
+        closedir(d);
+        std::sort(names.begin(), names.end());
+        if (names.empty())
+            fail(YLM_LOAD_ERROR, "Folder (%s) has no model weight files", dir.c_str());
+        for (auto &p : names)
+            add_file(p);
+    }
+
+    void add_file(const std::string &path)
+    {
+        auto f = std::make_unique<StFile>();
+        f->fd = ::open(path.c_str(), O_RDONLY);
+        if (f->fd < 0)
+            fail(YLM_LOAD_ERROR, "open failed: %s", path.c_str());
+        struct stat sb;
+        fstat(f->fd, &sb);
+        f->size = (size_t)sb.st_size;
+        if (f->size < 8)
+            fail(YLM_LOAD_ERROR, "bad safetensors file: %s", path.c_str());
+        f->map = mmap(nullptr, f->size, PROT_READ, MAP_PRIVATE, f->fd, 0);
+        if (f->map == MAP_FAILED)
+            fail(YLM_LOAD_ERROR, "mmap failed: %s", path.c_str());
+        const uint8_t *base = static_cast<const uint8_t *>(f->map);
+        uint64_t hlen;
+        memcpy(&hlen, base, 8);
+        if (hlen == 0 || hlen > (1ull << 30) || 8 + hlen > f->size)
+            fail(YLM_LOAD_ERROR, "bad header size in %s", path.c_str());
+        JVal h = json_parse(std::string(reinterpret_cast<const char *>(base + 8), hlen));
+        const uint8_t *data = base + 8 + hlen;
+        const size_t dsize = f->size - 8 - hlen;
+        for (auto &kv : h.obj)
+        {
+            const JVal &v = kv.second;
+            if (v.kind != JVal::Obj || !v.has("dtype") || !v.has("shape") || !v.has("data_offsets"))
+                continue;
+            StTensor t;
+            t.dtype = v.get("dtype")->str;
+            for (auto &s : v.get("shape")->arr)
+                t.shape.push_back((int64_t)s.as_num());
+            const auto &off = v.get("data_offsets")->arr;
+            const size_t o0 = (size_t)off.at(0).as_num(), o1 = (size_t)off.at(1).as_num();
+            if (o1 < o0 || o1 > dsize)
+                fail(YLM_LOAD_ERROR, "tensor %s out of file bounds", kv.first.c_str());
+            t.data = data + o0;
+            t.bytes = o1 - o0;
+            if (!tensors.count(kv.first))
+                tensors[kv.first] = t;
+        }
+        files.push_back(std::move(f));
+    }
+
+    const StTensor *find(const std::string &n) const
+    {
+        auto it = tensors.find(n);
+        return it == tensors.end() ? nullptr : &it->second;
+    }
+};
+
+int dtype_code(const std::string &d)
+{
+    if (d == "F16")
+        return 0;
+    if (d == "BF16")
+        return 1;
+    if (d == "F32")
+        return 2;
+    fail(YLM_LOAD_ERROR, "unsupported dtype %s", d.c_str());
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+} // namespace
+
+// ------------------------------------------------------------------ engine
+struct ylm_engine
+{
+    ylm_model_config cfg{};
+    ylm_engine_options opt{};
+    int dev = 0, sms = 148;
+    cudaStream_t st = nullptr;
+
+    int H = 0, L = 0, D = YLM_HEAD_DIM, Hq = 0, Hkv = 0, hq = 0, hkv = 0, I = 0, inter = 0, qkv_rows = 0;
+    int64_t V = 0, v_local = 0;
+    int tp = 1, rank = 0;
+
+    uint8_t *wblob = nullptr;
+    size_t wbytes = 0;
+    __half *emb = nullptr, *lm = nullptr, *fnorm = nullptr;
+    struct Layer
+    {
+        __half *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+        __half *ln1 = nullptr, *ln2 = nullptr, *qn = nullptr, *kn = nullptr;
+        GemvPlan pq, po, pgu, pd;
+    };
+    std::vector<Layer> layers;
+    GemvPlan plm;
+
+    __half *kc = nullptr, *vc = nullptr;
+    int cap = 0;
+    size_t kv_layer = 0; // elements per layer (one of K or V)
+    __half *rcos = nullptr, *rsin = nullptr;
+    int max_pos = 0;
+
+    // decode workspace
+    __half *x = nullptr, *x2 = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr, *logits = nullptr,
+           *logits_local = nullptr, *ar = nullptr;
+    float *partial = nullptr;
+    int *counters = nullptr;
+    int splits = 1;
+    StepState *dstate = nullptr, *hin = nullptr, *hout = nullptr;
+    uint64_t *cand = nullptr;
+    int *cand_count = nullptr, *smp_counter = nullptr;
+    int parts = 1;
+    int64_t *dbg_ids = nullptr;
+    float *dbg_probs = nullptr;
+    uint32_t *mask_bits = nullptr;
+
+    // prefill workspace
+    int pf_cap = 0;
+    __half *pX = nullptr, *pXn = nullptr, *pQKV = nullptr, *pQ = nullptr, *pO = nullptr, *pA = nullptr;
+    int64_t *pIds = nullptr;
+
+    cudaGraphExec_t g_fwd = nullptr, g_fwd_sample = nullptr;
+
+    bool ready = false;
+    int last = 0;
+    int max_seq = 0;
+    bool has_logits = false;
+
+    int greedy = 1, top_k = 40;
+    float temp = 0.6f;
+    uint64_t seed = 0;
+    float u_next = -1.f;
+    int64_t calls = 0;
+    int last_k = 0;
+
+    ncclComm_t comm = nullptr;
+    cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    double prefill_ms = 0.0;
+
+    ~ylm_engine() { release(); }
+
+    void release()
+    {
+        if (dev >= 0)
+            cudaSetDevice(dev);
+        if (g_fwd)
+            cudaGraphExecDestroy(g_fwd);
+        if (g_fwd_sample)
+            cudaGraphExecDestroy(g_fwd_sample);
+        g_fwd = g_fwd_sample = nullptr;
+        if (comm)
+            ncclCommDestroy(comm);
+        comm = nullptr;
+        if (ev_a)
+            cudaEventDestroy(ev_a);
+        if (ev_b)
+            cudaEventDestroy(ev_b);
+        ev_a = ev_b = nullptr;
+        for (void *p : {(void *)wblob, (void *)kc, (void *)vc, (void *)rcos, (void *)rsin, (void *)x, (void *)x2,
+                        (void *)qkv, (void *)att, (void *)act, (void *)logits, (void *)logits_local, (void *)ar,
+                        (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
+                        (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
+                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds})
+            if (p)
+                cudaFree(p);
+        wblob = nullptr;
+        kc = vc = nullptr;
+        if (hin)
+            cudaFreeHost(hin);
+        if (hout)
+            cudaFreeHost(hout);
+        hin = hout = nullptr;
+        if (st)
+            cudaStreamDestroy(st);
+        st = nullptr;
+    }
+
+    template <typename T> T *dalloc(size_t n)
+    {
+        void *p = nullptr;
+        CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+        CK(cudaMemset(p, 0, std::max<size_t>(n, 1) * sizeof(T)));
+        return static_cast<T *>(p);
+    }
+
+    // -------------------------------------------------------------- set-up
+    void init(const char *snapshot_dir, const ylm_model_config &c, const ylm_engine_options &o)
+    {
+        cfg = c;
+        opt = o;
+        dev = o.device;
+        tp = std::max(1, o.tp_size);
+        rank = o.tp_rank;
+        H = c.hidden_size;
+        L = c.num_layers;
+        Hq = c.num_heads;
+        Hkv = c.num_kv_heads;
+        I = c.intermediate_size;
+        V = c.vocab_size;
+        if (c.head_dim != YLM_HEAD_DIM)
+            fail(YLM_UNSUPPORTED, "head_dim %d: kernels are built for 128", c.head_dim);
+        if (H <= 0 || L <= 0 || Hq <= 0 || Hkv <= 0 || I <= 0 || V <= 0 || Hq % Hkv)
+            fail(YLM_INVALID_ARG, "invalid model shape");
+        if (Hq / Hkv > 8)
+            fail(YLM_UNSUPPORTED, "more than 8 query heads per KV head");
+        if (H % 8 || I % 8)
+            fail(YLM_UNSUPPORTED, "hidden and intermediate sizes must be multiples of 8");
+        if (rank < 0 || rank >= tp || Hkv % tp || I % tp || V % tp)
+            fail(YLM_INVALID_ARG, "tensor parallel %d does not divide KV heads, intermediate or vocab", tp);
+        hq = Hq / tp;
+        hkv = Hkv / tp;
+        inter = I / tp;
+        v_local = V / tp;
+        qkv_rows = (hq + 2 * hkv) * D;
+
+        CK(cudaSetDevice(dev));
+        CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        CK(kernels_prepare());
+        CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+
+        if (tp > 1)
+        {
+            if (!o.nccl_id)
+                fail(YLM_INVALID_ARG, "tp_size > 1 needs an NCCL unique id");
+            ncclUniqueId id;
+            memcpy(&id, o.nccl_id, sizeof(id));
+            NK(ncclCommInitRank(&comm, tp, id, rank));
+        }
+
+        alloc_weights();
+        if (snapshot_dir)
+            load_weights(snapshot_dir);
+        else
+            random_weights();
+        build_plans();
+        alloc_kv();
+        build_rope();
+        alloc_workspace();
+        compute_max_seq();
+        CK(cudaStreamSynchronize(st));
+    }
+
+    void alloc_weights()
+    {
+        const bool bias = cfg.model_type == YLM_MODEL_QWEN2_5;
+        const bool qkn = cfg.model_type == YLM_MODEL_QWEN3;
+        size_t off = 0;
+        auto take = [&](size_t elems) {
+            size_t o = off;
+            off = align_up(off + elems * 2, 256);
+            return o;
+        };
+        struct Off
+        {
+            size_t wqkv, bqkv, wo, wgu, wd, ln1, ln2, qn, kn;
+        };
+        std::vector<Off> lo(L);
+        const size_t o_emb = take((size_t)V * H);
+        const size_t o_fn = take(H);
+        const bool own_lm = !cfg.tie_word_embeddings || tp > 1;
+        const size_t o_lm = own_lm ? take((size_t)v_local * H) : 0;
+        for (int l = 0; l < L; l++)
+        {
+            lo[l].wqkv = take((size_t)qkv_rows * H);
+            lo[l].bqkv = bias ? take(qkv_rows) : SIZE_MAX;
+            lo[l].wo = take((size_t)H * hq * D);
+            lo[l].wgu = take((size_t)2 * inter * H);
+            lo[l].wd = take((size_t)H * inter);
+            lo[l].ln1 = take(H);
+            lo[l].ln2 = take(H);
+            lo[l].qn = qkn ? take(D) : SIZE_MAX;
+            lo[l].kn = qkn ? take(D) : SIZE_MAX;
+        }
+        wbytes = off;
+        CK(cudaMalloc(&wblob, wbytes));
+        auto P = [&](size_t o) { return o == SIZE_MAX ? nullptr : reinterpret_cast<__half *>(wblob + o); };
+        emb = P(o_emb);
+        fnorm = P(o_fn);
+        lm = own_lm ? P(o_lm) : emb;
+        layers.resize(L);
+        for (int l = 0; l < L; l++)
+        {
+            Layer &y = layers[l];
+            y.wqkv = P(lo[l].wqkv);
+            y.bqkv = P(lo[l].bqkv);
+            y.wo = P(lo[l].wo);
+            y.wgu = P(lo[l].wgu);
+            y.wd = P(lo[l].wd);
+            y.ln1 = P(lo[l].ln1);
+            y.ln2 = P(lo[l].ln2);
+            y.qn = P(lo[l].qn);
+            y.kn = P(lo[l].kn);
+        }
+    }
+
+    // Each destination block of a weight: rows [r0, r0+nr) and columns [c0, c0+nc)
+    // of the HF tensor `name`, written with row pitch `ld` (elements).
+    struct Piece
+    {
+        std::string name;
+        __half *dst;
+        int64_t r0, nr, c0, nc, ld;
+        bool ones; // norm weight
+    };
+
+    std::vector<Piece> pieces()
+    {
+        std::vector<Piece> ps;
+        const bool bias = cfg.model_type == YLM_MODEL_QWEN2_5;
+        const bool qkn = cfg.model_type == YLM_MODEL_QWEN3;
+        ps.push_back({"model.embed_tokens.weight", emb, 0, V, 0, H, H, false});
+        ps.push_back({"model.norm.weight", fnorm, 0, 1, 0, H, H, true});
+        if (lm != emb)
+        {
+            const char *nm = cfg.tie_word_embeddings ? "model.embed_tokens.weight" : "lm_head.weight";
+            ps.push_back({nm, lm, rank * v_local, v_local, 0, H, H, false});
+        }
+        for (int l = 0; l < L; l++)
+        {
+            const std::string p = "model.layers." + std::to_string(l) + ".";
+            Layer &y = layers[l];
+            const int64_t q0 = (int64_t)rank * hq * D, k0 = (int64_t)rank * hkv * D;
+            ps.push_back({p + "self_attn.q_proj.weight", y.wqkv, q0, hq * D, 0, H, H, false});
+            ps.push_back({p + "self_attn.k_proj.weight", y.wqkv + (size_t)hq * D * H, k0, hkv * D, 0, H, H, false});
+            ps.push_back({p + "self_attn.v_proj.weight", y.wqkv + (size_t)(hq + hkv) * D * H, k0, hkv * D, 0, H, H,
+                          false});
+            if (bias)
+            {
+                ps.push_back({p + "self_attn.q_proj.bias", y.bqkv, 0, 1, q0, hq * D, hq * D, false});
+                ps.push_back({p + "self_attn.k_proj.bias", y.bqkv + hq * D, 0, 1, k0, hkv * D, hkv * D, false});
+                ps.push_back({p + "self_attn.v_proj.bias", y.bqkv + (hq + hkv) * D, 0, 1, k0, hkv * D, hkv * D, false});
+            }
+            if (qkn)
+            {
+                ps.push_back({p + "self_attn.q_norm.weight", y.qn, 0, 1, 0, D, D, true});
+                ps.push_back({p + "self_attn.k_norm.weight", y.kn, 0, 1, 0, D, D, true});
+            }
+            ps.push_back({p + "self_attn.o_proj.weight", y.wo, 0, H, q0, hq * D, hq * D, false});
+            ps.push_back({p + "input_layernorm.weight", y.ln1, 0, 1, 0, H, H, true});
+            ps.push_back({p + "post_attention_layernorm.weight", y.ln2, 0, 1, 0, H, H, true});
+            // gate and up interleaved by row: row 2j = gate_j, row 2j+1 = up_j
+            const int64_t i0 = (int64_t)rank * inter;
+            ps.push_back({p + "mlp.gate_proj.weight", y.wgu, i0, inter, 0, H, 2 * (int64_t)H, false});
+            ps.push_back({p + "mlp.up_proj.weight", y.wgu + H, i0, inter, 0, H, 2 * (int64_t)H, false});
+            ps.push_back({p + "mlp.down_proj.weight", y.wd, 0, H, i0, inter, inter, false});
+        }
+        return ps;
+    }
+
+    void random_weights()
+    {
+        const double stdv = opt.init_std > 0 ? (double)opt.init_std : 0.02;
+        for (auto &p : pieces())
+        {
+            if (p.ones)
+            {
+                CK(fill_const_launch(p.dst, p.nc, 1.0f, st));
+                continue;
+            }
+            // full column count of the HF tensor: 1-D tensors (biases) are one row
+            int64_t full_cols;
+            if (p.name.find("o_proj") != std::string::npos)
+                full_cols = (int64_t)Hq * D;
+            else if (p.name.find("down_proj") != std::string::npos)
+                full_cols = I;
+            else if (p.name.find(".bias") != std::string::npos)
+                full_cols = p.name.find("q_proj") != std::string::npos ? (int64_t)Hq * D : (int64_t)Hkv * D;
+            else
+                full_cols = H;
+            const uint64_t key = mix64(opt.init_seed) ^ fnv1a64(p.name);
+            CK(fill_normal_launch(p.dst, p.nr, p.nc, p.ld, key, p.r0, p.c0, full_cols, stdv, st));
+        }
+    }
+
+    void load_weights(const char *dir)
+    {
+        Snapshot snap;
+        snap.open_dir(dir);
+        std::vector<__half> stage;
+        for (auto &p : pieces())
+        {
+            const StTensor *t = snap.find(p.name);
+            if (!t)
+                fail(YLM_LOAD_ERROR, "missing tensor %s", p.name.c_str());
+            const int dc = dtype_code(t->dtype);
+            const size_t es = dc == 2 ? 4 : 2;
+            int64_t rows = 1, cols = 1;
+            if (t->shape.size() == 2)
+            {
+                rows = t->shape[0];
+                cols = t->shape[1];
+            }
+            else if (t->shape.size() == 1)
+                cols = t->shape[0];
+            else
+                fail(YLM_LOAD_ERROR, "tensor %s: rank %zu", p.name.c_str(), t->shape.size());
+            if (p.r0 + p.nr > rows || p.c0 + p.nc > cols || (size_t)(rows * cols) * es != t->bytes)
+                fail(YLM_LOAD_ERROR, "tensor %s: shape does not match the model config", p.name.c_str());
+            const uint8_t *src = t->data + ((size_t)p.r0 * cols + p.c0) * es;
+            if (dc == 0)
+            {
+                CK(cudaMemcpy2D(p.dst, p.ld * 2, src, cols * 2, p.nc * 2, p.nr, cudaMemcpyHostToDevice));
+                continue;
+            }
+            // BF16 / F32 shards: convert on the host, one row band at a time
+            const int64_t band = std::max<int64_t>(1, (64 << 20) / (p.nc * 2));
+            for (int64_t r = 0; r < p.nr; r += band)
+            {
+                const int64_t nr = std::min(band, p.nr - r);
+                stage.resize((size_t)nr * p.nc);
+                for (int64_t i = 0; i < nr; i++)
+                    for (int64_t j = 0; j < p.nc; j++)
+                    {
+                        const uint8_t *e = src + ((size_t)(r + i) * cols + j) * es;
+                        float f;
+                        if (dc == 1)
+                        {
+                            uint32_t u = (uint32_t)(e[0] | (e[1] << 8)) << 16;
+                            memcpy(&f, &u, 4);
+                        }
+                        else
+                            memcpy(&f, e, 4);
+                        stage[(size_t)i * p.nc + j] = __float2half_rn(f);
+                    }
+                CK(cudaMemcpy2D(p.dst + (size_t)r * p.ld, p.ld * 2, stage.data(), p.nc * 2, p.nc * 2, nr,
+                                cudaMemcpyHostToDevice));
+            }
+        }
+    }
+
+    void build_plans()
+    {
+        for (auto &y : layers)
+        {
+            if (!gemv_make_plan(&y.pq, y.wqkv, qkv_rows, H, 0, sms) || !gemv_make_plan(&y.po, y.wo, H, hq * D, 0, sms) ||
+                !gemv_make_plan(&y.pgu, y.wgu, 2 * inter, H, 1, sms) || !gemv_make_plan(&y.pd, y.wd, H, inter, 0, sms))
+                fail(YLM_UNSUPPORTED, "GEMV plan failed (tensor map encode)");
+        }
+        if (!gemv_make_plan(&plm, lm, (int)v_local, H, 0, sms))
+            fail(YLM_UNSUPPORTED, "GEMV plan failed for lm_head");
+    }
+
+    // ModelBase::InitKVCache (ModelBase.cpp:340-370): capacity from the GB
+    // budget with BF16-sized slots; this rank holds its KV heads for every slot.
+    void alloc_kv()
+    {
+        const size_t total = (size_t)((double)std::max(1, opt.kv_cache_gb) * 1024.0 * 1024.0 * 1024.0);
+        const size_t per_token = (size_t)Hkv * D * 2;
+        cap = (int)((total / per_token) / (size_t)L / 2);
+        kv_layer = (size_t)hkv * cap * D;
+        kc = dalloc<__half>(kv_layer * L);
+        vc = dalloc<__half>(kv_layer * L);
+    }
+
+    // ModelBase::BuildRopeCache (ModelBase.cpp:372-394), half-width tables
+    // [max_pos][64] (the two halves of cat(freqs, freqs) are equal).
+    void build_rope()
+    {
+        max_pos = cfg.max_position_embeddings;
+        const int half = D / 2;
+        std::vector<float> inv(half);
+        for (int i = 0; i < half; i++)
+        {
+            const float e = (float)i / (float)half;
+            inv[i] = (float)(1.0 / std::pow((double)cfg.rope_theta, (double)e));
+        }
+        if (opt.rope_scaling && cfg.rope_factor > 0 && cfg.rope_orig_max_pos > 0)
+        {
+            // Llama 3.1 frequency scaling (published with the Llama 3.1 release)
+            const double f = cfg.rope_factor, lo = cfg.rope_low_freq, hi = cfg.rope_high_freq;
+            const double orig = cfg.rope_orig_max_pos;
+            const double lo_wl = orig / lo, hi_wl = orig / hi;
+            for (int i = 0; i < half; i++)
+            {
+                const double v = inv[i];
+                const double wl = 2.0 * M_PI / v;
+                double out = wl > lo_wl ? v / f : v;
+                if (wl <= lo_wl && wl >= hi_wl)
+                {
+                    const double sm = (orig / wl - lo) / (hi - lo);
+                    out = (1.0 - sm) * v / f + sm * v;
+                }
+                inv[i] = (float)out;
+            }
+        }
+        std::vector<__half> hc((size_t)max_pos * half), hs((size_t)max_pos * half);
+        for (int p = 0; p < max_pos; p++)
+            for (int i = 0; i < half; i++)
+            {
+                const float a = (float)p * inv[i];
+                hc[(size_t)p * half + i] = __float2half_rn((float)std::cos((double)a));
+                hs[(size_t)p * half + i] = __float2half_rn((float)std::sin((double)a));
+            }
+        rcos = dalloc<__half>(hc.size());
+        rsin = dalloc<__half>(hs.size());
+        CK(cudaMemcpy(rcos, hc.data(), hc.size() * 2, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(rsin, hs.data(), hs.size() * 2, cudaMemcpyHostToDevice));
+    }
+
+    void alloc_workspace()
+    {
+        x = dalloc<__half>(H);
+        x2 = dalloc<__half>(H);
+        qkv = dalloc<__half>(qkv_rows);
+        att = dalloc<__half>((size_t)hq * D);
+        act = dalloc<__half>(inter);
+        logits = dalloc<__half>(V);
+        logits_local = tp > 1 ? dalloc<__half>(v_local) : logits;
+        ar = dalloc<__half>(H);
+        splits = attn_default_splits(hkv, sms);
+        partial = dalloc<float>(attn_partial_floats(hq, splits));
+        counters = dalloc<int>(hkv);
+        dstate = dalloc<StepState>(1);
+        CK(cudaMallocHost(&hin, sizeof(StepState)));
+        CK(cudaMallocHost(&hout, sizeof(StepState)));
+        memset(hin, 0, sizeof(StepState));
+        memset(hout, 0, sizeof(StepState));
+        parts = sample_parts(V, sms);
+        cand = dalloc<uint64_t>((size_t)parts * 64);
+        cand_count = dalloc<int>(parts);
+        smp_counter = dalloc<int>(1);
+        dbg_ids = dalloc<int64_t>(64);
+        dbg_probs = dalloc<float>(64);
+    }
+
+    // ModelBase::CalculateMaxSequenceLength (ModelBase.cpp:312-338)
+    void compute_max_seq()
+    {
+        size_t fr = 0, to = 0;
+        CK(cudaMemGetInfo(&fr, &to));
+        const size_t per_tok = (size_t)Hq * D * 2 * 3 * L;
+        const long long by_mem = (long long)((double)fr * 0.8 / (double)per_tok);
+        max_seq = (int)std::min<long long>(cfg.max_position_embeddings, by_mem);
+        if (max_seq < 512)
+            fail(YLM_LOAD_ERROR, "GPU memory too low: runtime cannot support the minimum context of 512 tokens");
+    }
+
+    void ensure_prefill(int T)
+    {
+        if (T <= pf_cap)
+            return;
+        int n = std::max(T, 64);
+        for (void *p : {(void *)pX, (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds})
+            if (p)
+                cudaFree(p);
+        pX = dalloc<__half>((size_t)n * H);
+        pXn = dalloc<__half>((size_t)n * H);
+        pQKV = dalloc<__half>((size_t)n * qkv_rows);
+        pQ = dalloc<__half>((size_t)n * hq * D);
+        pO = dalloc<__half>((size_t)n * std::max(hq * D, H));
+        pA = dalloc<__half>((size_t)n * inter);
+        pIds = dalloc<int64_t>(n);
+        pf_cap = n;
+    }
+
+    // -------------------------------------------------------------- decode step
+    AttnArgs attn_args(int l)
+    {
+        AttnArgs a;
+        a.qkv = qkv;
+        a.q_norm = layers[l].qn;
+        a.k_norm = layers[l].kn;
+        a.eps = cfg.rms_eps;
+        a.rope_cos = rcos;
+        a.rope_sin = rsin;
+        a.max_pos = max_pos;
+        a.k_cache = kc + (size_t)l * kv_layer;
+        a.v_cache = vc + (size_t)l * kv_layer;
+        a.cap = cap;
+        a.hq = hq;
+        a.hkv = hkv;
+        a.splits = splits;
+        a.partial = partial;
+        a.counters = counters;
+        a.out = att;
+        a.state = dstate;
+        a.err = &dstate->err;
+        return a;
+    }
+
+    void enqueue_forward(bool sample)
+    {
+        const bool pdl = opt.use_pdl != 0;
+        int *err = &dstate->err;
+        for (int l = 0; l < L; l++)
+        {
+            Layer &y = layers[l];
+            GemvArgs a;
+            a.x = x;
+            a.norm_w = y.ln1;
+            a.eps = cfg.rms_eps;
+            a.emb = emb;
+            a.vocab = V;
+            a.state = dstate;
+            a.resid_out = x;
+            a.out = qkv;
+            a.bias = y.bqkv;
+            a.err = err;
+            CK(gemv_launch(y.pq, l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, a, st, pdl));
+            CK(attn_decode_launch(attn_args(l), st, pdl));
+            GemvArgs o;
+            o.x = att;
+            o.err = err;
+            if (tp == 1)
+            {
+                o.resid = x;
+                CK(gemv_launch(y.po, PRO_VEC, EPI_RESID, o, st, pdl));
+            }
+            else
+            {
+                o.out = ar;
+                CK(gemv_launch(y.po, PRO_VEC, EPI_STORE, o, st, pdl));
+                NK(ncclAllReduce(ar, ar, H, ncclHalf, ncclSum, comm, st));
+                CK(resid_add_launch(x, ar, H));
+            }
+            GemvArgs g;
+            g.x = x;
+            g.norm_w = y.ln2;
+            g.eps = cfg.rms_eps;
+            g.out = act;
+            g.err = err;
+            CK(gemv_launch(y.pgu, PRO_RMSNORM, EPI_SWIGLU, g, st, pdl));
+            GemvArgs d;
+            d.x = act;
+            d.err = err;
+            if (tp == 1)
+            {
+                d.resid = x;
+                CK(gemv_launch(y.pd, PRO_VEC, EPI_RESID, d, st, pdl));
+            }
+            else
+            {
+                d.out = ar;
+                CK(gemv_launch(y.pd, PRO_VEC, EPI_STORE, d, st, pdl));
+                NK(ncclAllReduce(ar, ar, H, ncclHalf, ncclSum, comm, st));
+                CK(resid_add_launch(x, ar, H));
+            }
+        }
+        GemvArgs f;
+        f.x = x;
+        f.norm_w = fnorm;
+        f.eps = cfg.rms_eps;
+        f.out = logits_local;
+        f.err = err;
+        CK(gemv_launch(plm, PRO_RMSNORM, EPI_STORE, f, st, pdl));
+        if (tp > 1)
+            NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
+        if (sample)
+            CK(sample_launch(sample_args(), st, pdl));
+    }
+
+    cudaError_t resid_add_launch(__half *xx, const __half *y, int64_t n)
+    {
+        return resid_add_rows_launch(xx, y, n, st);
+    }
+
+    SampleArgs sample_args()
+    {
+        SampleArgs s;
+        s.logits = logits;
+        s.vocab = V;
+        s.mask_bits = mask_bits;
+        s.state = dstate;
+        s.cand = cand;
+        s.cand_count = cand_count;
+        s.counter = smp_counter;
+        s.parts = parts;
+        s.dbg_ids = dbg_ids;
+        s.dbg_probs = dbg_probs;
+        s.err = &dstate->err;
+        return s;
+    }
+
+    cudaGraphExec_t capture(bool sample)
+    {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+        try
+        {
+            enqueue_forward(sample);
+        }
+        catch (...)
+        {
+            cudaStreamEndCapture(st, &g);
+            if (g)
+                cudaGraphDestroy(g);
+            throw;
+        }
+        CK(cudaStreamEndCapture(st, &g));
+        cudaGraphExec_t ex = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        CK(e);
+        return ex;
+    }
+
+    void launch_forward(bool sample)
+    {
+        if (opt.use_cuda_graph)
+        {
+            cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
+            if (!ex)
+                ex = capture(sample);
+            CK(cudaGraphLaunch(ex, st));
+        }
+        else
+            enqueue_forward(sample);
+    }
+
+    void fill_state(int64_t token, int slot, int pos, bool do_greedy, int advance)
+    {
+        hin->token = token;
+        hin->next_token = -1;
+        hin->sample_calls = calls;
+        hin->slot = slot;
+        hin->rope_pos = pos;
+        hin->err = 0;
+        hin->greedy = do_greedy ? 1 : 0;
+        hin->top_k = std::max(1, std::min(top_k, 64));
+        hin->inv_temp = 1.0f / temp;
+        hin->u_override = u_next;
+        hin->advance = advance;
+        hin->seed = seed;
+        hin->u_used = -1.f;
+    }
+
+    void push_state() { CK(cudaMemcpyAsync(dstate, hin, sizeof(StepState), cudaMemcpyHostToDevice, st)); }
+
+    void pull_state_sync()
+    {
+        CK(cudaMemcpyAsync(hout, dstate, sizeof(StepState), cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        check_dev_err();
+    }
+
+    void check_dev_err()
+    {
+        if (hout->err != 0)
+        {
+            const int e = hout->err;
+            // counters may be left mid-step: reset them so the next step starts clean
+            cudaMemsetAsync(counters, 0, sizeof(int) * hkv, st);
+            cudaMemsetAsync(smp_counter, 0, sizeof(int), st);
+            cudaStreamSynchronize(st);
+            if (e == YLM_DEV_ERR_BAD_TOKEN)
+                fail(YLM_INVALID_ARG, "token id out of range");
+            if (e == YLM_DEV_ERR_BAD_STATE)
+                fail(YLM_INVALID_ARG, "slot or RoPE position out of range");
+            fail(YLM_DEVICE_TIMEOUT, "device wait expired (code %d)", e);
+        }
+    }
+
+    // -------------------------------------------------------------- prefill
+    void run_prefill(int T)
+    {
+        const float eps = cfg.rms_eps;
+        int *err = &dstate->err;
+        CK(embed_rows_launch(pIds, T, emb, V, H, pX, err, st));
+        for (int l = 0; l < L; l++)
+        {
+            Layer &y = layers[l];
+            __half *kl = kc + (size_t)l * kv_layer, *vl = vc + (size_t)l * kv_layer;
+            CK(rmsnorm_rows_launch(pX, y.ln1, eps, T, H, pXn, st));
+            CK(gemm_launch(pXn, H, y.wqkv, T, qkv_rows, H, GEMM_STORE, y.bqkv, pQKV, qkv_rows, st));
+            QkvPostArgs q;
+            q.qkv = pQKV;
+            q.q_norm = y.qn;
+            q.k_norm = y.kn;
+            q.eps = eps;
+            q.rope_cos = rcos;
+            q.rope_sin = rsin;
+            q.q_out = pQ;
+            q.k_cache = kl;
+            q.v_cache = vl;
+            q.cap = cap;
+            q.hq = hq;
+            q.hkv = hkv;
+            q.T = T;
+            q.pos0 = 0;
+            CK(qkv_post_prefill_launch(q, st));
+            CK(attn_prefill_launch(pQ, kl, vl, cap, hq, hkv, T, pO, st));
+            if (tp == 1)
+                CK(gemm_launch(pO, hq * D, y.wo, T, H, hq * D, GEMM_RESID, nullptr, pX, H, st));
+            else
+            {
+                CK(gemm_launch(pO, hq * D, y.wo, T, H, hq * D, GEMM_STORE, nullptr, pXn, H, st));
+                NK(ncclAllReduce(pXn, pXn, (size_t)T * H, ncclHalf, ncclSum, comm, st));
+                CK(resid_add_launch(pX, pXn, T * H));
+            }
+            CK(rmsnorm_rows_launch(pX, y.ln2, eps, T, H, pXn, st));
+            CK(gemm_launch(pXn, H, y.wgu, T, 2 * inter, H, GEMM_SWIGLU, nullptr, pA, inter, st));
+            if (tp == 1)
+                CK(gemm_launch(pA, inter, y.wd, T, H, inter, GEMM_RESID, nullptr, pX, H, st));
+            else
+            {
+                CK(gemm_launch(pA, inter, y.wd, T, H, inter, GEMM_STORE, nullptr, pXn, H, st));
+                NK(ncclAllReduce(pXn, pXn, (size_t)T * H, ncclHalf, ncclSum, comm, st));
+                CK(resid_add_launch(pX, pXn, T * H));
+            }
+        }
+        GemvArgs f;
+        f.x = pX + (size_t)(T - 1) * H;
+        f.norm_w = fnorm;
+        f.eps = eps;
+        f.out = logits_local;
+        f.err = err;
+        CK(gemv_launch(plm, PRO_RMSNORM, EPI_STORE, f, st, false));
+        if (tp > 1)
+            NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
+    }
+
+    // -------------------------------------------------------------- Model::Infer
+    // ModelBase::Infer (ModelBase.cpp:396-471) without its per-op launches.
+    int infer(int64_t *ids, int32_t *n_ids, int32_t *eos, int32_t *n_eos)
+    {
+        if (!ready)
+            fail(YLM_NOT_READY, "Call BeginInfer() first");
+        if (!ids || !n_ids || *n_ids <= 0)
+            fail(YLM_INVALID_ARG, "empty input");
+        // EnsureSequenceLength (ModelBase.cpp:473-505)
+        int n = *n_ids;
+        int ne = (eos && n_eos) ? *n_eos : 0;
+        while (n > max_seq)
+        {
+            int drop = 1;
+            if (ne > 0)
+            {
+                drop = eos[0] + 1;
+                for (int i = 1; i < ne; i++)
+                    eos[i - 1] = eos[i] - drop;
+                ne--;
+            }
+            drop = std::min(drop, n);
+            memmove(ids, ids + drop, sizeof(int64_t) * (n - drop));
+            n -= drop;
+        }
+        *n_ids = n;
+        if (n_eos)
+            *n_eos = ne;
+        if (n <= 0)
+            fail(YLM_INVALID_ARG, "empty input after trimming");
+
+        const bool kv = opt.kv_cache_enabled != 0;
+        if (last == 0)
+        {
+            // prefill, or every call with the KV cache off (ModelBase.cpp:539-565);
+            // with the cache off it still serves as the K/V workspace
+            if (n > cap - last)
+                return YLM_KV_CACHE_EXCEEDED;
+            if (n > max_pos)
+                fail(YLM_SEQUENCE_LENGTH_EXCEEDED, "prompt longer than the RoPE table");
+            ensure_prefill(n);
+            hin->err = 0;
+            fill_state(0, 0, 0, true, 0);
+            push_state();
+            CK(cudaMemcpyAsync(pIds, ids, sizeof(int64_t) * n, cudaMemcpyHostToDevice, st));
+            if (!ev_a)
+            {
+                CK(cudaEventCreate(&ev_a));
+                CK(cudaEventCreate(&ev_b));
+            }
+            CK(cudaEventRecord(ev_a, st));
+            run_prefill(n);
+            CK(cudaEventRecord(ev_b, st));
+            pull_state_sync();
+            float pf = 0.f;
+            CK(cudaEventElapsedTime(&pf, ev_a, ev_b));
+            prefill_ms = pf;
+            if (kv)
+                last = n - 1;
+        }
+        else
+        {
+            // decode (ModelBase.cpp:566-586)
+            if (n != 1)
+                fail(YLM_INVALID_ARG, "decode takes one token per call");
+            if (last + 1 > cap - last)
+                return YLM_KV_CACHE_EXCEEDED;
+            const int slot = last + 1;
+            const int pos = opt.rope_compat ? last : last + 1;
+            if (pos >= max_pos)
+                fail(YLM_SEQUENCE_LENGTH_EXCEEDED, "position beyond the RoPE table");
+            fill_state(ids[0], slot, pos, true, 0);
+            push_state();
+            launch_forward(false);
+            pull_state_sync();
+            last++;
+        }
+        has_logits = true;
+        return YLM_OK;
+    }
+
+    int64_t sample(bool do_greedy)
+    {
+        if (!has_logits)
+            fail(YLM_NOT_READY, "no logits to sample");
+        fill_state(0, 0, 0, do_greedy, 0);
+        push_state();
+        CK(sample_launch(sample_args(), st, false));
+        pull_state_sync();
+        note_sample(do_greedy);
+        return hout->next_token;
+    }
+
+    void note_sample(bool do_greedy)
+    {
+        calls++;
+        u_next = -1.f;
+        last_k = do_greedy ? 0 : std::max(1, std::min(top_k, 64));
+    }
+
+    // one decode step + sample (one graph launch)
+    int decode(int64_t id, bool do_greedy, int64_t *next)
+    {
+        if (!ready)
+            fail(YLM_NOT_READY, "Call BeginInfer() first");
+        if (last == 0)
+        {
+            // the reference treats this call as a prefill (P6: one-token prompt)
+            int64_t ids1[1] = {id};
+            int32_t n1 = 1;
+            int r = infer(ids1, &n1, nullptr, nullptr);
+            if (r != YLM_OK)
+                return r;
+            *next = sample(do_greedy);
+            return YLM_OK;
+        }
+        if (last + 1 > cap - last)
+            return YLM_KV_CACHE_EXCEEDED;
+        const int slot = last + 1;
+        const int pos = opt.rope_compat ? last : last + 1;
+        if (pos >= max_pos)
+            fail(YLM_SEQUENCE_LENGTH_EXCEEDED, "position beyond the RoPE table");
+        fill_state(id, slot, pos, do_greedy, 0);
+        push_state();
+        launch_forward(true);
+        pull_state_sync();
+        last++;
+        has_logits = true;
+        note_sample(do_greedy);
+        *next = hout->next_token;
+        return YLM_OK;
+    }
+
+    void begin()
+    {
+        ready = true;
+        last = 0;
+        has_logits = false;
+        if (opt.zero_kv_on_begin && opt.kv_cache_enabled)
+        {
+            CK(cudaMemsetAsync(kc, 0, kv_layer * L * 2, st));
+            CK(cudaMemsetAsync(vc, 0, kv_layer * L * 2, st));
+            CK(cudaStreamSynchronize(st));
+        }
+    }
+};
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+const char *ylm_status_string(int s)
+{
+    switch (s)
+    {
+    case YLM_OK: return "ok";
+    case YLM_SEQUENCE_LENGTH_EXCEEDED: return "sequence length exceeded";
+    case YLM_KV_CACHE_EXCEEDED: return "KV cache capacity exceeded";
+    case YLM_INVALID_PROMPT: return "invalid prompt";
+    case YLM_CANCELED: return "canceled";
+    case YLM_GPU_QUEUE_TIMED_OUT: return "GPU queue timed out";
+    case YLM_INVALID_ARG: return "invalid argument";
+    case YLM_NOT_READY: return "not ready (call ylm_begin_infer first)";
+    case YLM_LOAD_ERROR: return "load error";
+    case YLM_CUDA_ERROR: return "CUDA error";
+    case YLM_DEVICE_TIMEOUT: return "device wait timed out";
+    case YLM_COMM_ERROR: return "communication error";
+    case YLM_UNSUPPORTED: return "unsupported";
+    default: return "unknown status";
+    }
+}
+
+const char *ylm_last_error(void) { return g_last_error.c_str(); }
+
+int ylm_options_default(ylm_engine_options *o)
+{
+    if (!o)
+        return YLM_INVALID_ARG;
+    memset(o, 0, sizeof(*o));
+    o->kv_cache_gb = 2;
+    o->kv_cache_enabled = 1;
+    o->rope_compat = 1;
+    o->rope_scaling = 0;
+    o->use_cuda_graph = 1;
+    o->use_pdl = 1;
+    o->tp_size = 1;
+    o->init_std = 0.02f;
+    o->zero_kv_on_begin = 1;
+    return YLM_OK;
+}
+
+int ylm_config_from_json(const char *path, ylm_model_config *c)
+{
+    return guarded([&]() -> int {
+        if (!path || !c)
+            fail(YLM_INVALID_ARG, "null argument");
+        JVal j = json_parse(read_file(path));
+        memset(c, 0, sizeof(*c));
+        auto num = [&](const char *k) -> double {
+            const JVal *v = j.get(k);
+            if (!v)
+                fail(YLM_LOAD_ERROR, "config.json: missing %s", k);
+            return v->as_num();
+        };
+        const JVal *mt = j.get("model_type");
+        if (!mt)
+            fail(YLM_LOAD_ERROR, "config.json: missing model_type");
+        std::string t = mt->str;
+        for (auto &ch : t)
+            ch = (char)tolower(ch);
+        if (t == "llama")
+            c->model_type = YLM_MODEL_LLAMA;
+        else if (t == "mistral")
+            c->model_type = YLM_MODEL_MISTRAL;
+        else if (t == "qwen2")
+            c->model_type = YLM_MODEL_QWEN2_5;
+        else if (t == "qwen3")
+            c->model_type = YLM_MODEL_QWEN3;
+        else
+            fail(YLM_LOAD_ERROR, "Unsupported model type: %s", t.c_str());
+        c->num_layers = (int)num("num_hidden_layers");
+        c->hidden_size = (int)num("hidden_size");
+        c->num_heads = (int)num("num_attention_heads");
+        c->num_kv_heads = (int)num("num_key_value_heads");
+        c->vocab_size = (int64_t)num("vocab_size");
+        c->rms_eps = (float)num("rms_norm_eps");
+        c->rope_theta = (float)num("rope_theta");
+        c->max_position_embeddings = (int)num("max_position_embeddings");
+        c->intermediate_size = (int)num("intermediate_size");
+        c->head_dim = j.has("head_dim") ? (int)num("head_dim") : c->hidden_size / std::max(1, c->num_heads);
+        const JVal *tie = j.get("tie_word_embeddings");
+        c->tie_word_embeddings = tie ? (tie->kind == JVal::Bool ? tie->b : tie->as_num() != 0) : 0;
+        c->rope_factor = 1.f;
+        c->rope_low_freq = 1.f;
+        c->rope_high_freq = 1.f;
+        c->rope_orig_max_pos = c->max_position_embeddings;
+        if (const JVal *rs = j.get("rope_scaling"))
+            if (rs->kind == JVal::Obj)
+            {
+                if (rs->has("factor"))
+                    c->rope_factor = (float)rs->get("factor")->as_num();
+                if (rs->has("low_freq_factor"))
+                    c->rope_low_freq = (float)rs->get("low_freq_factor")->as_num();
+                if (rs->has("high_freq_factor"))
+                    c->rope_high_freq = (float)rs->get("high_freq_factor")->as_num();
+                if (rs->has("original_max_position_embeddings"))
+                    c->rope_orig_max_pos = (int)rs->get("original_max_position_embeddings")->as_num();
+            }
+        if (const JVal *e = j.get("eos_token_id"))
+        {
+            if (e->kind == JVal::Arr)
+                for (auto &v : e->arr)
+                {
+                    if (c->n_eos < 8)
+                        c->eos_ids[c->n_eos++] = (int)v.as_num();
+                }
+            else if (e->kind == JVal::Num)
+                c->eos_ids[c->n_eos++] = (int)e->num;
+        }
+        if (c->hidden_size % std::max(1, c->num_heads))
+            fail(YLM_LOAD_ERROR, "HiddenSize must be divisible by NumHeads");
+        return YLM_OK;
+    });
+}
+
+int ylm_resolve_snapshot(const char *root, char *out, int32_t out_len)
+{
+    return guarded([&]() -> int {
+        if (!root || !out || out_len <= 0)
+            fail(YLM_INVALID_ARG, "null argument");
+        std::string ref = std::string(root) + "/refs/main";
+        std::ifstream f(ref);
+        if (!f)
+            fail(YLM_LOAD_ERROR, "Invalid HuggingFace repo: refs/main not found in %s", root);
+        std::string h;
+        std::getline(f, h);
+        std::string snap = std::string(root) + "/snapshots/" + h;
+        struct stat sb;
+        if (stat(snap.c_str(), &sb) != 0)
+            fail(YLM_LOAD_ERROR, "Snapshot folder does not exist: %s", snap.c_str());
+        if ((int)snap.size() + 1 > out_len)
+            fail(YLM_INVALID_ARG, "output buffer too small");
+        memcpy(out, snap.c_str(), snap.size() + 1);
+        return YLM_OK;
+    });
+}
+
+int ylm_nccl_unique_id(void *out128)
+{
+    return guarded([&]() -> int {
+        if (!out128)
+            fail(YLM_INVALID_ARG, "null argument");
+        ncclUniqueId id;
+        NK(ncclGetUniqueId(&id));
+        memcpy(out128, &id, sizeof(id));
+        return YLM_OK;
+    });
+}
+
+int ylm_create(const char *snapshot_dir, const ylm_model_config *cfg, const ylm_engine_options *opt, ylm_engine **out)
+{
+    return guarded([&]() -> int {
+        if (!cfg || !out)
+            fail(YLM_INVALID_ARG, "null argument");
+        ylm_engine_options o;
+        if (opt)
+            o = *opt;
+        else
+            ylm_options_default(&o);
+        auto e = std::make_unique<ylm_engine>();
+        e->init(snapshot_dir, *cfg, o);
+        *out = e.release();
+        return YLM_OK;
+    });
+}
+
+int ylm_destroy(ylm_engine *e)
+{
+    delete e;
+    return YLM_OK;
+}
+
+int ylm_begin_infer(ylm_engine *e)
+{
+    return guarded([&]() -> int {
+        if (!e)
+            fail(YLM_INVALID_ARG, "null engine");
+        CK(cudaSetDevice(e->dev));
+        e->begin();
+        return YLM_OK;
+    });
+}
+
+int ylm_infer(ylm_engine *e, int64_t *ids, int32_t *n_ids, int32_t *eos, int32_t *n_eos)
+{
+    return guarded([&]() -> int {
+        if (!e)
+            fail(YLM_INVALID_ARG, "null engine");
+        CK(cudaSetDevice(e->dev));
+        return e->infer(ids, n_ids, eos, n_eos);
+    });
+}
+
+int ylm_logits(ylm_engine *e, void *host_out, int32_t as_float32)
+{
+    return guarded([&]() -> int {
+        if (!e || !host_out)
+            fail(YLM_INVALID_ARG, "null argument");
+        if (!e->has_logits)
+            fail(YLM_NOT_READY, "no logits yet");
+        CK(cudaSetDevice(e->dev));
+        if (!as_float32)
+        {
+            CK(cudaMemcpyAsync(host_out, e->logits, e->V * 2, cudaMemcpyDeviceToHost, e->st));
+            CK(cudaStreamSynchronize(e->st));
+            return YLM_OK;
+        }
+        std::vector<__half> tmp(e->V);
+        CK(cudaMemcpyAsync(tmp.data(), e->logits, e->V * 2, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        float *o = static_cast<float *>(host_out);
+        for (int64_t i = 0; i < e->V; i++)
+            o[i] = __half2float(tmp[i]);
+        return YLM_OK;
+    });
+}
+
+int ylm_logits_device(ylm_engine *e, const void **dev_ptr, int64_t *vocab)
+{
+    if (!e || !dev_ptr)
+        return YLM_INVALID_ARG;
+    *dev_ptr = e->logits;
+    if (vocab)
+        *vocab = e->V;
+    return YLM_OK;
+}
+
+int ylm_set_sampling(ylm_engine *e, const ylm_sampling *s)
+{
+    return guarded([&]() -> int {
+        if (!e || !s)
+            fail(YLM_INVALID_ARG, "null argument");
+        if (!s->greedy && (s->top_k < 1 || s->top_k > 64 || !(s->temperature > 0.f)))
+            fail(YLM_INVALID_ARG, "top_k must be in 1..64 and temperature > 0");
+        CK(cudaSetDevice(e->dev));
+        e->greedy = s->greedy;
+        e->top_k = s->top_k;
+        e->temp = s->temperature > 0.f ? s->temperature : 1.f;
+        e->seed = s->seed;
+        // special-token mask bitmap (ChatSession.cpp:41-61)
+        if (e->mask_bits)
+        {
+            cudaFree(e->mask_bits);
+            e->mask_bits = nullptr;
+        }
+        if (s->n_masked > 0 && s->masked_ids)
+        {
+            std::vector<uint32_t> bits((e->V + 31) / 32, 0u);
+            for (int i = 0; i < s->n_masked; i++)
+            {
+                const int64_t id = s->masked_ids[i];
+                if (id >= 0 && id < e->V)
+                    bits[id >> 5] |= 1u << (id & 31);
+            }
+            e->mask_bits = e->dalloc<uint32_t>(bits.size());
+            CK(cudaMemcpy(e->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice));
+        }
+        // the graph with the sampler bakes in the mask pointer: rebuild it
+        if (e->g_fwd_sample)
+        {
+            cudaGraphExecDestroy(e->g_fwd_sample);
+            e->g_fwd_sample = nullptr;
+        }
+        return YLM_OK;
+    });
+}
+
+int ylm_sample(ylm_engine *e, int32_t greedy, int64_t *next_id)
+{
+    return guarded([&]() -> int {
+        if (!e || !next_id)
+            fail(YLM_INVALID_ARG, "null argument");
+        CK(cudaSetDevice(e->dev));
+        *next_id = e->sample(greedy != 0);
+        return YLM_OK;
+    });
+}
+
+int ylm_decode(ylm_engine *e, int64_t id, int32_t greedy, int64_t *next_id)
+{
+    return guarded([&]() -> int {
+        if (!e || !next_id)
+            fail(YLM_INVALID_ARG, "null argument");
+        CK(cudaSetDevice(e->dev));
+        return e->decode(id, greedy != 0, next_id);
+    });
+}
+
+int ylm_generate(ylm_engine *e, const int64_t *prompt, int32_t n_prompt, int32_t max_new, const int64_t *eos_ids,
+                 int32_t n_eos, int64_t *out_ids, int32_t *n_out, double *first_ms, double *decode_ms)
+{
+    return guarded([&]() -> int {
+        if (!e || !prompt || n_prompt <= 0 || !out_ids || !n_out || max_new < 0)
+            fail(YLM_INVALID_ARG, "bad argument");
+        CK(cudaSetDevice(e->dev));
+        using clk = std::chrono::steady_clock;
+        *n_out = 0;
+        double t_first = 0, t_dec = 0;
+        e->begin();
+        std::vector<int64_t> ids(prompt, prompt + n_prompt);
+        int generated = 0;
+        int64_t next = -1;
+        int status = YLM_OK;
+        const bool kv = e->opt.kv_cache_enabled != 0;
+        while (generated < max_new)
+        {
+            auto t0 = clk::now();
+            int r;
+            if (generated == 0 || !kv || e->last == 0)
+            {
+                int32_t n = (int32_t)ids.size();
+                r = e->infer(ids.data(), &n, nullptr, nullptr);
+                ids.resize(n);
+                if (r == YLM_OK)
+                    next = e->sample(e->greedy || generated == 0); // ChatSession.cpp:140
+            }
+            else
+                r = e->decode(next, e->greedy != 0, &next);
+            auto t1 = clk::now();
+            if (r != YLM_OK)
+            {
+                status = r;
+                break;
+            }
+            const double dt = std::chrono::duration<double, std::milli>(t1 - t0).count();
+            if (generated == 0)
+                t_first = dt;
+            else
+                t_dec += dt;
+            generated++;
+            // stop rules of ChatSession.cpp:151-161: an EOS id, or prompt + generated
+            // reaching MaxSequenceLength; the token that ends the loop is not emitted
+            bool end = std::find(eos_ids, eos_ids + n_eos, next) != eos_ids + n_eos;
+            if (!end && n_prompt + generated >= e->max_seq)
+                end = true;
+            if (end)
+                break;
+            out_ids[(*n_out)++] = next;
+            if (!kv)
+                ids.push_back(next);
+        }
+        if (first_ms)
+            *first_ms = t_first;
+        if (decode_ms)
+            *decode_ms = t_dec;
+        return status;
+    });
+}
+
+int ylm_set_draw(ylm_engine *e, float u)
+{
+    if (!e)
+        return YLM_INVALID_ARG;
+    e->u_next = u;
+    return YLM_OK;
+}
+
+int ylm_last_topk(ylm_engine *e, int64_t *ids, float *probs, int32_t *k, float *u)
+{
+    return guarded([&]() -> int {
+        if (!e)
+            fail(YLM_INVALID_ARG, "null engine");
+        CK(cudaSetDevice(e->dev));
+        if (k)
+            *k = e->last_k;
+        if (u)
+            *u = e->hout->u_used;
+        if (e->last_k > 0)
+        {
+            if (ids)
+                CK(cudaMemcpy(ids, e->dbg_ids, sizeof(int64_t) * e->last_k, cudaMemcpyDeviceToHost));
+            if (probs)
+                CK(cudaMemcpy(probs, e->dbg_probs, sizeof(float) * e->last_k, cudaMemcpyDeviceToHost));
+        }
+        return YLM_OK;
+    });
+}
+
+int ylm_info(ylm_engine *e, int32_t *kv_capacity, int32_t *last_kv_index, int32_t *max_seq_len)
+{
+    if (!e)
+        return YLM_INVALID_ARG;
+    if (kv_capacity)
+        *kv_capacity = e->cap;
+    if (last_kv_index)
+        *last_kv_index = e->last;
+    if (max_seq_len)
+        *max_seq_len = e->max_seq;
+    return YLM_OK;
+}
+
+int ylm_last_prefill_ms(ylm_engine *e, double *ms)
+{
+    if (!e || !ms)
+        return YLM_INVALID_ARG;
+    *ms = e->prefill_ms;
+    return YLM_OK;
+}
+
+int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
+{
+    return guarded([&]() -> int {
+        if (!e || iters <= 0 || !ms_per_step)
+            fail(YLM_INVALID_ARG, "bad argument");
+        if (!e->ready || e->last == 0)
+            fail(YLM_NOT_READY, "run a prefill first");
+        // every step must pass the decode capacity rule last + 1 <= cap - last
+        if (2 * (e->last + iters) - 1 > e->cap || e->last + iters >= e->max_pos)
+            return (int)YLM_KV_CACHE_EXCEEDED;
+        CK(cudaSetDevice(e->dev));
+        // device-side chaining: the sampler writes the next token and advances slot/pos
+        e->fill_state(0, e->last + 1, e->opt.rope_compat ? e->last : e->last + 1, e->greedy != 0, 1);
+        e->hin->token = e->hout->next_token >= 0 ? e->hout->next_token : 0;
+        e->push_state();
+        if (!e->g_fwd_sample)
+            e->g_fwd_sample = e->capture(true);
+        cudaEvent_t a, b;
+        CK(cudaEventCreate(&a));
+        CK(cudaEventCreate(&b));
+        CK(cudaEventRecord(a, e->st));
+        for (int i = 0; i < iters; i++)
+            CK(cudaGraphLaunch(e->g_fwd_sample, e->st));
+        CK(cudaEventRecord(b, e->st));
+        CK(cudaEventSynchronize(b));
+        float ms = 0;
+        CK(cudaEventElapsedTime(&ms, a, b));
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        e->pull_state_sync();
+        e->last += iters;
+        e->calls += iters;
+        *ms_per_step = ms / iters;
+        return YLM_OK;
+    });
+}
+
+} // extern "C"

@@ -1,0 +1,177 @@
+// Kernel parameter blocks and launchers shared by the engine and the kernels.
+// Host-side declarations only; no torch types anywhere.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#define YLM_HEAD_DIM 128
+
+// Device-side error words (written with atomicExch, read by the host after a step).
+#define YLM_DEV_ERR_NONE 0
+#define YLM_DEV_ERR_TIMEOUT_FULL 1
+#define YLM_DEV_ERR_TIMEOUT_EMPTY 2
+#define YLM_DEV_ERR_TIMEOUT_DRAIN 3
+#define YLM_DEV_ERR_BAD_TOKEN 4
+#define YLM_DEV_ERR_BAD_STATE 5
+#define YLM_DEV_ERR_TIMEOUT_PEER 6
+
+namespace ylm {
+
+// Per-engine device-resident step state. The decode graph reads the token,
+// slot and RoPE position from here, so one captured graph serves every step.
+struct StepState
+{
+    int64_t token;        // input token of the decode step
+    int64_t next_token;   // sampler output
+    int64_t sample_calls; // sampler calls so far (Philox counter)
+    int32_t slot;         // KV slot written this step
+    int32_t rope_pos;     // RoPE position of this step's token
+    int32_t err;          // device error word (YLM_DEV_ERR_*)
+    int32_t greedy;       // 1: argmax; 0: top-k + temperature
+    int32_t top_k;        // 1..64
+    float inv_temp;       // 1/temperature (FP32)
+    float u_override;     // >= 0: uniform draw to use instead of Philox (tests)
+    int32_t advance;      // 1: after sampling, token=next, slot++, rope_pos++
+    uint64_t seed;        // Philox key
+    float u_used;         // the uniform the last top-k draw used
+    int32_t pad;
+};
+
+// ------------------------------------------------------------------ GEMV
+enum GemvPro
+{
+    PRO_VEC = 0,          // input vector as is
+    PRO_RMSNORM = 1,      // RMSNorm(x) * w of the residual stream
+    PRO_EMBED_RMSNORM = 2 // x = embedding[state.token]; CTA 0 writes x to resid_out
+};
+enum GemvEpi
+{
+    EPI_STORE = 0, // out[row] = fp16(y) (+ bias, rounded again)
+    EPI_RESID = 1, // resid[row] = fp16(resid[row] + fp16(y))
+    EPI_SWIGLU = 2 // rows (2p, 2p+1) = (gate_p, up_p): out[p] = fp16(fp16(silu(g)) * u)
+};
+
+struct GemvPlan
+{
+    CUtensorMap map;
+    const __half *w;
+    int N, K;       // rows, columns of W
+    int rb;         // rows per block (TMA box height)
+    int n_blocks;   // ceil(N / rb)
+    int grid;       // CTAs
+    int nst;        // pipeline stages
+    int k_pad;      // K rounded up to 256
+    int pair;       // 1: SwiGLU row pairs
+    size_t smem;    // dynamic shared memory bytes
+};
+
+struct GemvArgs
+{
+    const __half *x = nullptr;      // input vector (PRO_VEC) or residual stream (PRO_RMSNORM)
+    const __half *norm_w = nullptr; // RMSNorm weight [K]
+    float eps = 0.f;
+    const __half *emb = nullptr;    // PRO_EMBED_RMSNORM: embedding [V, K]
+    int64_t vocab = 0;
+    const StepState *state = nullptr;
+    __half *resid_out = nullptr;    // PRO_EMBED_RMSNORM: x written here by CTA 0
+    __half *out = nullptr;
+    const __half *bias = nullptr;
+    __half *resid = nullptr;
+    int *err = nullptr;
+};
+
+bool gemv_make_plan(GemvPlan *plan, const __half *w, int N, int K, int pair, int num_sms);
+cudaError_t gemv_launch(const GemvPlan &plan, int pro, int epi, const GemvArgs &a, cudaStream_t s, bool pdl);
+cudaError_t gemv_prepare();
+
+// ------------------------------------------------------------------ decode attention
+struct AttnArgs
+{
+    const __half *qkv;    // [ (hq + 2 hkv) * 128 ]: q heads, k heads, v heads
+    const __half *q_norm; // [128] or null (Qwen3 q/k RMSNorm)
+    const __half *k_norm;
+    float eps;
+    const __half *rope_cos; // [max_pos][64]
+    const __half *rope_sin;
+    int max_pos;
+    __half *k_cache; // this layer, [hkv][cap][128]
+    __half *v_cache;
+    int cap;
+    int hq, hkv;
+    int splits;
+    float *partial; // [hq][splits][2 + 128]
+    int *counters;  // [hkv], zero between launches
+    __half *out;    // [hq * 128]
+    const StepState *state;
+    int *err;
+};
+size_t attn_partial_floats(int hq, int splits);
+int attn_default_splits(int hkv, int num_sms);
+cudaError_t attn_decode_launch(const AttnArgs &a, cudaStream_t s, bool pdl);
+cudaError_t attn_prepare();
+
+// ------------------------------------------------------------------ sampler
+struct SampleArgs
+{
+    const __half *logits;
+    int64_t vocab;
+    const uint32_t *mask_bits; // V bits, 1 = masked special id; null = none
+    StepState *state;
+    uint64_t *cand;   // [parts][64]
+    int *cand_count;  // [parts]
+    int *counter;     // zero between launches
+    int parts;
+    int64_t *dbg_ids; // [64] final top-k ids in sampling order (or null)
+    float *dbg_probs; // [64]
+    int *err;
+};
+int sample_parts(int64_t vocab, int num_sms);
+cudaError_t sample_launch(const SampleArgs &a, cudaStream_t s, bool pdl);
+cudaError_t sample_prepare();
+
+// Shared-memory opt-in of every kernel on the current device (idempotent).
+cudaError_t kernels_prepare();
+
+// ------------------------------------------------------------------ prefill (T tokens)
+cudaError_t embed_rows_launch(const int64_t *ids, int T, const __half *emb, int64_t vocab, int H, __half *x, int *err,
+                              cudaStream_t s);
+cudaError_t rmsnorm_rows_launch(const __half *x, const __half *w, float eps, int T, int H, __half *y, cudaStream_t s);
+
+enum GemmEpi
+{
+    GEMM_STORE = 0,
+    GEMM_RESID = 1,
+    GEMM_SWIGLU = 2
+};
+// C[T, N] = A[T, K] x W[N, K]^T with epilogue; A row stride lda, C row stride ldc.
+cudaError_t gemm_launch(const __half *A, int lda, const __half *W, int T, int N, int K, int epi, const __half *bias,
+                        __half *C, int ldc, cudaStream_t s);
+
+struct QkvPostArgs
+{
+    const __half *qkv; // [T][(hq + 2 hkv) * 128]
+    const __half *q_norm, *k_norm;
+    float eps;
+    const __half *rope_cos, *rope_sin;
+    __half *q_out; // [T][hq * 128]
+    __half *k_cache, *v_cache;
+    int cap, hq, hkv, T, pos0;
+};
+cudaError_t qkv_post_prefill_launch(const QkvPostArgs &a, cudaStream_t s);
+// x[i] = fp16(x[i] + y[i]) (residual add after a tensor-parallel all-reduce)
+cudaError_t resid_add_rows_launch(__half *x, const __half *y, int64_t n, cudaStream_t s);
+// causal attention over KV slots [0, T): q [T][hq*128] -> out [T][hq*128]
+cudaError_t attn_prefill_launch(const __half *q, const __half *k_cache, const __half *v_cache, int cap, int hq,
+                                int hkv, int T, __half *out, cudaStream_t s);
+
+// ------------------------------------------------------------------ init
+// dst[r * ld + c] = N(0, std) element ((row0 + r) * full_cols + col0 + c) of stream `key`
+cudaError_t fill_normal_launch(__half *dst, int64_t rows, int64_t cols, int64_t ld, uint64_t key, int64_t row0,
+                               int64_t col0, int64_t full_cols, double stdv, cudaStream_t s);
+cudaError_t fill_const_launch(__half *dst, int64_t n, float v, cudaStream_t s);
+cudaError_t convert_to_half_launch(const void *src, int src_dtype, __half *dst, int64_t n, cudaStream_t s);
+
+} // namespace ylm
