@@ -234,6 +234,7 @@ def gemv_roofline(spec, hbm_peak, peak_kind):
     iters = 64
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    torch.cuda._sleep(1000000)  # keep the stream busy while the launches are queued
     a.record(s)
     for i in range(iters):
         L.ylm_k_gemv(ctypes.c_void_p(ws[i % 4].data_ptr()), n, k, ctypes.c_void_p(x.data_ptr()),

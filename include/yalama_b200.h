@@ -86,8 +86,9 @@ typedef struct ylm_engine_options {
     int32_t tp_size;          /* tensor-parallel ranks (1, 2, 4, 8); one engine per rank */
     const void *nccl_id;      /* 128-byte NCCL unique id from ylm_nccl_unique_id on rank 0 */
     uint64_t init_seed;       /* snapshot_dir == NULL: seeded N(0, init_std) weights, norms 1.0 */
-    float init_std;
+    double init_std;
     int32_t zero_kv_on_begin; /* 1 (default): BeginInfer zeroes the cache like ModelBase.cpp:302-309 */
+    int32_t prefill_tensor_cores; /* 1 (default): tcgen05 GEMMs for prefill; 0: CUDA-core GEMMs */
 } ylm_engine_options;
 
 /* ChatSession::Sample parameters (src/ChatSession.cpp:560-593). */
@@ -165,8 +166,10 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step);
 /* ---- kernel-level entry points (device pointers; stream = cudaStream_t or NULL) */
 /* y[n] = W[n,k] x[k], FP16 in and out, FP32 accumulation (the decode GEMV). */
 int ylm_k_gemv(const void *w, int32_t n, int32_t k, const void *x, void *y, void *stream);
-/* C[t,n] = A[t,k] W[n,k]^T, FP16 (the prefill GEMM). */
-int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, void *c, void *stream);
+/* C[t,n] = A[t,k] W[n,k]^T, FP16 (the prefill GEMM): tensor_cores = 1 the
+ * tcgen05 kernel, 0 the CUDA-core kernel. */
+int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, void *c, int32_t tensor_cores,
+               void *stream);
 /* One decode-attention step for one layer: q/k-norm (optional), RoPE at rope_pos,
  * append k/v at `slot`, attention over slots [0, slot]. qkv: [(hq+2hkv)*128];
  * rope tables [max_pos][64]; caches [hkv][cap][128]; out [hq*128]. */

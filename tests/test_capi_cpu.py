@@ -45,6 +45,7 @@ int main(void) {
   printf("ylm_sampling %zu\n", sizeof(ylm_sampling));
   P(ylm_model_config, vocab_size) P(ylm_model_config, eos_ids) P(ylm_model_config, n_eos)
   P(ylm_engine_options, nccl_id) P(ylm_engine_options, init_seed) P(ylm_engine_options, zero_kv_on_begin)
+  P(ylm_engine_options, prefill_tensor_cores) P(ylm_engine_options, init_std)
   P(ylm_sampling, seed) P(ylm_sampling, masked_ids) P(ylm_sampling, n_masked)
   return 0;
 }
@@ -112,7 +113,7 @@ def test_kernel_entry_points_validate_arguments():
     L = E.lib()
     # rejected before touching any device
     assert L.ylm_k_gemv(None, 4, 8, None, None, None) == E.Status.INVALID_ARG
-    assert L.ylm_k_gemm(None, None, 1, 1, 1, None, None) == E.Status.INVALID_ARG
+    assert L.ylm_k_gemm(None, None, 1, 1, 1, None, 1, None) == E.Status.INVALID_ARG
     assert L.ylm_k_sample(None, 10, 1, 1, 1.0, None, 0.5, None, None, None, None) == E.Status.INVALID_ARG
     assert L.ylm_k_decode_attention(None, None, None, 1e-6, None, None, 16, None, None, 8, 4, 2, 0, 0, None,
                                     None) == E.Status.INVALID_ARG

@@ -9,7 +9,10 @@
 
 #include <cuda_runtime.h>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <tuple>
 
 using namespace ylm;
 
@@ -53,19 +56,49 @@ int ylm_k_gemv(const void *w, int32_t n, int32_t k, const void *x, void *y, void
         return YLM_INVALID_ARG;
     if (prepare_device() != cudaSuccess)
         return YLM_CUDA_ERROR;
+    // plans (tensor map + tiling) are cached per (device, weight, shape)
+    static std::mutex mu;
+    static std::map<std::tuple<int, const void *, int, int>, GemvPlan> plans;
+    int dev = 0;
+    cudaGetDevice(&dev);
     GemvPlan plan;
-    if (!gemv_make_plan(&plan, static_cast<const __half *>(w), n, k, 0, sm_count()))
-        return YLM_UNSUPPORTED;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto key = std::make_tuple(dev, w, n, k);
+        auto it = plans.find(key);
+        if (it == plans.end())
+        {
+            if (!gemv_make_plan(&plan, static_cast<const __half *>(w), n, k, 0, sm_count()))
+                return YLM_UNSUPPORTED;
+            if (plans.size() > 4096)
+                plans.clear();
+            plans[key] = plan;
+        }
+        else
+            plan = it->second;
+    }
     GemvArgs a;
     a.x = static_cast<const __half *>(x);
     a.out = static_cast<__half *>(y);
     return cuda_status(gemv_launch(plan, PRO_VEC, EPI_STORE, a, static_cast<cudaStream_t>(stream), false));
 }
 
-int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, void *c, void *stream)
+int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, void *c, int32_t tensor_cores,
+               void *stream)
 {
     if (!a || !w || !c || t <= 0 || n <= 0 || k <= 0)
         return YLM_INVALID_ARG;
+    if (prepare_device() != cudaSuccess)
+        return YLM_CUDA_ERROR;
+    if (tensor_cores)
+    {
+        CUtensorMap am, wm;
+        if (!tc_make_a_map(&am, static_cast<const __half *>(a), t, k, k) ||
+            !tc_make_w_map(&wm, static_cast<const __half *>(w), n, k))
+            return YLM_UNSUPPORTED;
+        return cuda_status(gemm_tc_launch(am, wm, t, n, k, GEMM_STORE, nullptr, static_cast<__half *>(c), n, nullptr,
+                                          static_cast<cudaStream_t>(stream)));
+    }
     return cuda_status(gemm_launch(static_cast<const __half *>(a), k, static_cast<const __half *>(w), t, n, k,
                                    GEMM_STORE, nullptr, static_cast<__half *>(c), n,
                                    static_cast<cudaStream_t>(stream)));

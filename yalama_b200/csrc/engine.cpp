@@ -260,6 +260,7 @@ struct ylm_engine
         __half *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
         __half *ln1 = nullptr, *ln2 = nullptr, *qn = nullptr, *kn = nullptr;
         GemvPlan pq, po, pgu, pd;
+        CUtensorMap tq, to, tgu, td; // tcgen05 operand maps of the four weights
     };
     std::vector<Layer> layers;
     GemvPlan plm;
@@ -519,7 +520,7 @@ struct ylm_engine
 
     void random_weights()
     {
-        const double stdv = opt.init_std > 0 ? (double)opt.init_std : 0.02;
+        const double stdv = opt.init_std > 0 ? opt.init_std : 0.02;
         for (auto &p : pieces())
         {
             if (p.ones)
@@ -608,6 +609,10 @@ struct ylm_engine
         }
         if (!gemv_make_plan(&plm, lm, (int)v_local, H, 0, sms))
             fail(YLM_UNSUPPORTED, "GEMV plan failed for lm_head");
+        for (auto &y : layers)
+            if (!tc_make_w_map(&y.tq, y.wqkv, qkv_rows, H) || !tc_make_w_map(&y.to, y.wo, H, hq * D) ||
+                !tc_make_w_map(&y.tgu, y.wgu, 2 * inter, H) || !tc_make_w_map(&y.td, y.wd, H, inter))
+                fail(YLM_UNSUPPORTED, "tensor map encode failed for a prefill weight");
     }
 
     // ModelBase::InitKVCache (ModelBase.cpp:340-370): capacity from the GB
@@ -921,17 +926,31 @@ struct ylm_engine
     }
 
     // -------------------------------------------------------------- prefill
+    // one prefill GEMM: tcgen05 (default) or CUDA cores
+    void pgemm(const __half *A, const CUtensorMap &am, int lda, const __half *W, const CUtensorMap &wm, int T, int N,
+               int K, int epi, const __half *bias, __half *C, int ldc)
+    {
+        if (opt.prefill_tensor_cores)
+            CK(gemm_tc_launch(am, wm, T, N, K, epi, bias, C, ldc, &dstate->err, st));
+        else
+            CK(gemm_launch(A, lda, W, T, N, K, epi, bias, C, ldc, st));
+    }
+
     void run_prefill(int T)
     {
         const float eps = cfg.rms_eps;
         int *err = &dstate->err;
+        CUtensorMap m_xn, m_o, m_a;
+        if (!tc_make_a_map(&m_xn, pXn, T, H, H) || !tc_make_a_map(&m_o, pO, T, hq * D, hq * D) ||
+            !tc_make_a_map(&m_a, pA, T, inter, inter))
+            fail(YLM_UNSUPPORTED, "tensor map encode failed for a prefill activation");
         CK(embed_rows_launch(pIds, T, emb, V, H, pX, err, st));
         for (int l = 0; l < L; l++)
         {
             Layer &y = layers[l];
             __half *kl = kc + (size_t)l * kv_layer, *vl = vc + (size_t)l * kv_layer;
             CK(rmsnorm_rows_launch(pX, y.ln1, eps, T, H, pXn, st));
-            CK(gemm_launch(pXn, H, y.wqkv, T, qkv_rows, H, GEMM_STORE, y.bqkv, pQKV, qkv_rows, st));
+            pgemm(pXn, m_xn, H, y.wqkv, y.tq, T, qkv_rows, H, GEMM_STORE, y.bqkv, pQKV, qkv_rows);
             QkvPostArgs q;
             q.qkv = pQKV;
             q.q_norm = y.qn;
@@ -950,20 +969,20 @@ struct ylm_engine
             CK(qkv_post_prefill_launch(q, st));
             CK(attn_prefill_launch(pQ, kl, vl, cap, hq, hkv, T, pO, st));
             if (tp == 1)
-                CK(gemm_launch(pO, hq * D, y.wo, T, H, hq * D, GEMM_RESID, nullptr, pX, H, st));
+                pgemm(pO, m_o, hq * D, y.wo, y.to, T, H, hq * D, GEMM_RESID, nullptr, pX, H);
             else
             {
-                CK(gemm_launch(pO, hq * D, y.wo, T, H, hq * D, GEMM_STORE, nullptr, pXn, H, st));
+                pgemm(pO, m_o, hq * D, y.wo, y.to, T, H, hq * D, GEMM_STORE, nullptr, pXn, H);
                 NK(ncclAllReduce(pXn, pXn, (size_t)T * H, ncclHalf, ncclSum, comm, st));
                 CK(resid_add_launch(pX, pXn, T * H));
             }
             CK(rmsnorm_rows_launch(pX, y.ln2, eps, T, H, pXn, st));
-            CK(gemm_launch(pXn, H, y.wgu, T, 2 * inter, H, GEMM_SWIGLU, nullptr, pA, inter, st));
+            pgemm(pXn, m_xn, H, y.wgu, y.tgu, T, 2 * inter, H, GEMM_SWIGLU, nullptr, pA, inter);
             if (tp == 1)
-                CK(gemm_launch(pA, inter, y.wd, T, H, inter, GEMM_RESID, nullptr, pX, H, st));
+                pgemm(pA, m_a, inter, y.wd, y.td, T, H, inter, GEMM_RESID, nullptr, pX, H);
             else
             {
-                CK(gemm_launch(pA, inter, y.wd, T, H, inter, GEMM_STORE, nullptr, pXn, H, st));
+                pgemm(pA, m_a, inter, y.wd, y.td, T, H, inter, GEMM_STORE, nullptr, pXn, H);
                 NK(ncclAllReduce(pXn, pXn, (size_t)T * H, ncclHalf, ncclSum, comm, st));
                 CK(resid_add_launch(pX, pXn, T * H));
             }
@@ -1164,8 +1183,9 @@ int ylm_options_default(ylm_engine_options *o)
     o->use_cuda_graph = 1;
     o->use_pdl = 1;
     o->tp_size = 1;
-    o->init_std = 0.02f;
+    o->init_std = 0.02;
     o->zero_kv_on_begin = 1;
+    o->prefill_tensor_cores = 1;
     return YLM_OK;
 }
 

@@ -1,0 +1,319 @@
+// Prefill GEMM on the 5th-generation tensor cores: C[T, N] = A[T, K] W[N, K]^T,
+// FP16 operands, FP32 accumulation in tensor memory, FP16 output with the
+// reference's epilogue roundings (bias, residual add, SwiGLU), replacing the
+// prompt-wide torch::matmul calls of the reference's prefill
+// (src/models/ModelBase.cpp:763, 772, 781, 838, 744-750).
+//
+// One CTA computes a 128 x 256 output tile:
+//   warp 0      TMA producer: A box [128 x 64] and W box [256 x 64] per stage
+//               (128-byte swizzle, no multicast), 4 stages, mbarrier ring
+//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma
+//               (M=128, N=256, K=16, kind::f16, both operands K-major) and
+//               tcgen05.commit frees each stage and finally signals the epilogue
+//   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, 32 columns at a
+//               time, epilogue op, FP16 stores
+// Every wait is bounded; on expiry the kernel records an error, drains its own
+// copies and MMAs, releases TMEM and returns.
+#include "ylm_common.cuh"
+#include "ylm_kernels.h"
+#include <cudaTypedefs.h>
+
+namespace ylm {
+
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_ST = 4;
+constexpr int TC_THREADS = 192;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2; // 16 KB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2; // 32 KB
+constexpr int TC_TMEM_COLS = 256;
+constexpr size_t TC_SMEM = 1024 + (size_t)TC_ST * (TC_A_BYTES + TC_B_BYTES) + 256;
+
+struct TcArgs
+{
+    int T, N, K, epi;
+    const __half *bias;
+    __half *C;
+    int ldc;
+    int *err;
+};
+
+// K-major operand tile in shared memory with the 128-byte swizzle: rows of 64
+// FP16 (128 B), 8-row atoms of 1024 B (stride byte offset), SM100 descriptor
+// version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc_k128(uint32_t saddr)
+{
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D FP32, A/B FP16, both K-major, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t tc_idesc(int m, int n)
+{
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+                 "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v)
+{
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                   "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                   "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                   "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+        v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const TcArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sa = smem;
+    uint8_t *sb = smem + (size_t)TC_ST * TC_A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sb + (size_t)TC_ST * TC_B_BYTES);
+    uint64_t *empty = full + TC_ST;
+    uint64_t *accum = empty + TC_ST;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
+    int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
+    const int KT = (p.K + TC_BK - 1) / TC_BK;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < TC_ST; s++)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            prefetch_tensormap(&amap);
+            prefetch_tensormap(&wmap);
+            int issued = 0;
+            for (int kt = 0; kt < KT; kt++)
+            {
+                const int s = kt % TC_ST;
+                if (kt >= TC_ST && !mbar_wait_bounded(&empty[s], ((kt / TC_ST) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                {
+                    *abort_flag = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], TC_A_BYTES + TC_B_BYTES);
+                tma_load_2d(sa + (size_t)s * TC_A_BYTES, &amap, kt * TC_BK, m0, &full[s]);
+                tma_load_2d(sb + (size_t)s * TC_B_BYTES, &wmap, kt * TC_BK, n0, &full[s]);
+                issued++;
+            }
+            for (int kt = issued > TC_ST ? issued - TC_ST : 0; kt < issued; kt++)
+                mbar_wait_bounded(&full[kt % TC_ST], (kt / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            const uint32_t idesc = tc_idesc(TC_BM, TC_BN);
+            for (int kt = 0; kt < KT; kt++)
+            {
+                const int s = kt % TC_ST;
+                if (!mbar_wait_bounded(&full[s], (kt / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sa + (size_t)s * TC_A_BYTES);
+                const uint32_t b0 = smem_u32(sb + (size_t)s * TC_B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < TC_BK / 16; kk++)
+                    tc_mma(tmem, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
+                           (kt | kk) != 0 ? 1u : 0u);
+                tc_commit(&empty[s]); // stage free once these MMAs have read it
+            }
+            tc_commit(accum); // all issued MMAs complete -> epilogue
+        }
+        __syncwarp();
+    }
+    else
+    {
+        // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        const bool ok = mbar_wait_bounded(accum, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
+        tc_fence_after();
+        if (ok && !*abort_flag)
+        {
+            for (int c0 = 0; c0 < TC_BN; c0 += 32)
+            {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                const int col0 = n0 + c0;
+                if (row >= p.T || col0 >= p.N)
+                    continue;
+                __half *crow = p.C + (int64_t)row * p.ldc;
+                if (p.epi == GEMM_SWIGLU)
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2)
+                    {
+                        const int col = col0 + j;
+                        if (col < p.N)
+                        {
+                            const float g = rh(v[j]), u = rh(v[j + 1]);
+                            const float sg = rh(g / (1.0f + expf(-g)));
+                            crow[col >> 1] = f2h(sg * u);
+                        }
+                    }
+                }
+                else if (p.epi == GEMM_RESID)
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if (col0 + j < p.N)
+                            crow[col0 + j] = f2h(h2f(crow[col0 + j]) + rh(v[j]));
+                }
+                else
+                {
+                    if (col0 + 32 <= p.N && !p.bias)
+                    {
+                        uint4 pk[4];
+                        __half2 *h = reinterpret_cast<__half2 *>(pk);
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                        uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            dst[j] = pk[j];
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N)
+                            {
+                                float y = v[j];
+                                if (p.bias)
+                                    y = rh(y) + h2f(p.bias[col0 + j]);
+                                crow[col0 + j] = f2h(y);
+                            }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn)
+    {
+        cudaDriverEntryPointQueryResult q;
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+// K-major FP16 operand [rows, K] with row stride ld (elements), box [box_rows x 64], 128-byte swizzle.
+bool tc_make_operand_map(CUtensorMap *map, const __half *p, int rows, int K, int ld, int box_rows)
+{
+    auto enc = encoder();
+    if (!enc || (ld % 8) || (reinterpret_cast<uintptr_t>(p) % 16) || rows <= 0 || K <= 0)
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(p), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_make_a_map(CUtensorMap *map, const __half *A, int T, int K, int lda)
+{
+    return tc_make_operand_map(map, A, T, K, lda, TC_BM);
+}
+
+bool tc_make_w_map(CUtensorMap *map, const __half *W, int N, int K)
+{
+    return tc_make_operand_map(map, W, N, K, K, TC_BN);
+}
+
+cudaError_t gemm_tc_prepare()
+{
+    return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+}
+
+cudaError_t gemm_tc_launch(const CUtensorMap &amap, const CUtensorMap &wmap, int T, int N, int K, int epi,
+                           const __half *bias, __half *C, int ldc, int *err, cudaStream_t s)
+{
+    if (T <= 0)
+        return cudaSuccess;
+    TcArgs a;
+    a.T = T;
+    a.N = N;
+    a.K = K;
+    a.epi = epi;
+    a.bias = bias;
+    a.C = C;
+    a.ldc = ldc;
+    a.err = err;
+    dim3 grid((N + TC_BN - 1) / TC_BN, (T + TC_BM - 1) / TC_BM);
+    gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(amap, wmap, a);
+    return cudaGetLastError();
+}
+
+} // namespace ylm

@@ -92,6 +92,8 @@ cudaError_t kernels_prepare()
         e = attn_prepare();
     if (e == cudaSuccess)
         e = sample_prepare();
+    if (e == cudaSuccess)
+        e = gemm_tc_prepare();
     return e;
 }
 

@@ -150,6 +150,14 @@ enum GemmEpi
 cudaError_t gemm_launch(const __half *A, int lda, const __half *W, int T, int N, int K, int epi, const __half *bias,
                         __half *C, int ldc, cudaStream_t s);
 
+// Tensor-core (tcgen05) GEMM with the same epilogues. Operand maps: A [T, K]
+// (row stride lda) and W [N, K], both FP16 K-major, built once per buffer.
+bool tc_make_a_map(CUtensorMap *map, const __half *A, int T, int K, int lda);
+bool tc_make_w_map(CUtensorMap *map, const __half *W, int N, int K);
+cudaError_t gemm_tc_launch(const CUtensorMap &amap, const CUtensorMap &wmap, int T, int N, int K, int epi,
+                           const __half *bias, __half *C, int ldc, int *err, cudaStream_t s);
+cudaError_t gemm_tc_prepare();
+
 struct QkvPostArgs
 {
     const __half *qkv; // [T][(hq + 2 hkv) * 128]

@@ -85,8 +85,9 @@ class EngineOptions(ctypes.Structure):
         ("tp_size", ctypes.c_int32),
         ("nccl_id", ctypes.c_void_p),
         ("init_seed", ctypes.c_uint64),
-        ("init_std", ctypes.c_float),
+        ("init_std", ctypes.c_double),
         ("zero_kv_on_begin", ctypes.c_int32),
+        ("prefill_tensor_cores", ctypes.c_int32),
     ]
 
 
@@ -140,7 +141,7 @@ SIGNATURES = {
     "ylm_time_decode": (ctypes.c_int, [_P, ctypes.c_int32, _F64P]),
     "ylm_last_prefill_ms": (ctypes.c_int, [_P, _F64P]),
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
-    "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P]),
+    "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_decode_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, _P, _P]),
