@@ -81,7 +81,8 @@ typedef struct ylm_engine_options {
     int32_t rope_scaling;     /* 1: apply llama3 frequency scaling (the reference parses it,
                                  ConfigManager.cpp:448-463, but BuildRopeCache ignores it) */
     int32_t use_cuda_graph;   /* 1 (default): one graph launch per decode step */
-    int32_t use_pdl;          /* 1 (default): programmatic dependent launch between kernels */
+    int32_t use_pdl;          /* programmatic dependent launch: 1 between all decode kernels,
+                                 2 only into the projections, 0 (default) off */
     int32_t tp_rank;
     int32_t tp_size;          /* tensor-parallel ranks (1, 2, 4, 8); one engine per rank */
     const void *nccl_id;      /* 128-byte NCCL unique id from ylm_nccl_unique_id on rank 0 */

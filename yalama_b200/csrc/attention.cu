@@ -8,14 +8,14 @@
 // here the query heads of one KV group share a single read of that group's K/V.
 //
 // Grid: (KV head, split). Each CTA owns a contiguous token range of one KV head
-// and all G = hq/hkv query heads of the group. K/V rows of earlier steps are
-// constant during the step, so thread 0 bulk-copies them (cp.async.bulk, 256 B
-// per token, no multicast) into a ring of shared-memory tiles before
-// griddepcontrol.wait; the new token's k/v are computed from the QKV output and
-// used from shared memory. Half-warps take one token each (16 lanes x 8
-// elements of D), online softmax in FP32 (base 2), partials per split go to a
-// scratch buffer and the last CTA of each KV head combines them and writes the
-// FP16 attention output [hq * 128].
+// and all G = hq/hkv query heads of the group. Half-warps take one token at a
+// time (16 lanes x 8 elements of D, one 16-byte streaming load of K and one of
+// V per lane), ATT_UT tokens per half-warp in flight, online softmax in FP32
+// (base 2). K/V rows of earlier steps are constant during the step, so the
+// first group of loads is issued before griddepcontrol.wait; the new token's
+// k/v are computed from the QKV output and used from shared memory. Partials
+// per split go to a scratch buffer and the last CTA of each KV head (atomic
+// ticket) combines them and writes the FP16 attention output [hq * 128].
 #include "ylm_common.cuh"
 #include "ylm_kernels.h"
 #include <algorithm>
@@ -23,9 +23,10 @@
 namespace ylm {
 
 constexpr int ATT_THREADS = 128;
-constexpr int ATT_TT = 32;  // tokens per tile
-constexpr int ATT_NST = 4;  // tiles in flight
+constexpr int ATT_HW = ATT_THREADS / 16; // half-warps
+constexpr int ATT_UT = 4;                // tokens in flight per half-warp
 constexpr int ATT_ROW = 2 + YLM_HEAD_DIM;
+constexpr int ATT_MIN_SPLIT = 64;        // tokens per split, at least
 constexpr float ATT_SCALE_LOG2 = 0.08838834764831845f * 1.4426950408889634f;
 
 // One warp prepares one head: optional per-head RMSNorm, then RoPE at `pos`.
@@ -87,21 +88,26 @@ __device__ __forceinline__ void att_update(float &m, float &l, float *o, float s
     m = mn;
 }
 
+__device__ __forceinline__ uint4 ldg_nc(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 template <int G>
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs a)
 {
-    extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int TILE_BYTES = ATT_TT * YLM_HEAD_DIM * 2;
-    uint8_t *tiles = smem; // ATT_NST x (K tile, V tile)
-    float *q_s = reinterpret_cast<float *>(smem + ATT_NST * 2 * TILE_BYTES);
-    float *kn_s = q_s + G * YLM_HEAD_DIM;
-    float *vn_s = kn_s + YLM_HEAD_DIM;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(vn_s + YLM_HEAD_DIM);
-    int *flags = reinterpret_cast<int *>(bars + ATT_NST); // [0] abort, [1] ticket, [2] tiles issued
-    float *merge = reinterpret_cast<float *>(tiles); // aliases the tiles after the token loop
+    __shared__ float q_s[G * YLM_HEAD_DIM];
+    __shared__ float kn_s[YLM_HEAD_DIM], vn_s[YLM_HEAD_DIM];
+    __shared__ float merge[ATT_HW * G * ATT_ROW];
+    __shared__ int ticket;
 
     const int g = blockIdx.x, sp = blockIdx.y, S = gridDim.y;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hw = tid >> 4, l16 = tid & 15;
 
     pdl_launch_dependents();
     const int slot = a.state->slot;
@@ -113,37 +119,34 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
         return;
     }
     const int n = slot + 1;
-    const int chunk = (n + S - 1) / S;
-    const int t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk);
+    // at least ATT_MIN_SPLIT tokens per split: short contexts use fewer splits
+    // (the rest of the grid exits at once) and a cheaper combine
+    const int chunk = max(ATT_MIN_SPLIT, (n + S - 1) / S);
+    const int S_eff = (n + chunk - 1) / chunk;
+    if (sp >= S_eff)
+        return;
+    const int t0 = sp * chunk, t1 = min(n, t0 + chunk);
     const bool owns_new = slot >= t0 && slot < t1;
-    const int te = owns_new ? slot : t1;
-    const int n_tiles = (te - t0 + ATT_TT - 1) / ATT_TT;
-    const __half *kc = a.k_cache + (size_t)g * a.cap * YLM_HEAD_DIM;
-    const __half *vc = a.v_cache + (size_t)g * a.cap * YLM_HEAD_DIM;
+    const int te = owns_new ? slot : t1; // cached tokens [t0, te); the new one comes from qkv
+    const __half *kc = a.k_cache + (size_t)g * a.cap * YLM_HEAD_DIM + l16 * 8;
+    const __half *vc = a.v_cache + (size_t)g * a.cap * YLM_HEAD_DIM + l16 * 8;
 
-    auto issue = [&](int i) {
-        const int s = i % ATT_NST;
-        const int ta = t0 + i * ATT_TT;
-        const int nt = min(ATT_TT, te - ta);
-        const uint32_t bytes = nt * YLM_HEAD_DIM * 2;
-        mbar_arrive_expect_tx(&bars[s], 2 * bytes);
-        bulk_load(tiles + (size_t)s * 2 * TILE_BYTES, kc + (size_t)ta * YLM_HEAD_DIM, bytes, &bars[s]);
-        bulk_load(tiles + (size_t)s * 2 * TILE_BYTES + TILE_BYTES, vc + (size_t)ta * YLM_HEAD_DIM, bytes, &bars[s]);
-        flags[2] = i + 1; // tiles issued so far (thread 0 only)
+    // token i of this half-warp's sequence: t0 + hw + ATT_HW * i
+    uint4 kr[ATT_UT], vr[ATT_UT];
+    auto load_group = [&](int i0) {
+#pragma unroll
+        for (int u = 0; u < ATT_UT; u++)
+        {
+            const int t = t0 + hw + ATT_HW * (i0 + u);
+            if (t < te)
+            {
+                kr[u] = ldg_nc(kc + (size_t)t * YLM_HEAD_DIM);
+                vr[u] = ldg_nc(vc + (size_t)t * YLM_HEAD_DIM);
+            }
+        }
     };
-
-    if (tid == 0)
-    {
-        for (int s = 0; s < ATT_NST; s++)
-            mbar_init(&bars[s], 1);
-        flags[0] = 0;
-        flags[2] = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0)
-        for (int i = 0; i < min(ATT_NST, n_tiles); i++)
-            issue(i);
+    // earlier slots are constant during this step: start their loads before the wait
+    load_group(0);
 
     // ---- wait for the QKV projection, then prepare q (and the new k, v)
     pdl_wait();
@@ -173,8 +176,6 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
     }
     __syncthreads();
 
-    // ---- token loop: half-warp hw takes tokens hw, hw+8, ... of each tile
-    const int hw = tid >> 4, l16 = tid & 15;
     float q[G][8], o[G][8], m[G], l[G];
 #pragma unroll
     for (int h = 0; h < G; h++)
@@ -188,59 +189,44 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
         m[h] = -INFINITY;
         l[h] = 0.f;
     }
-    bool ok = true;
-    for (int i = 0; i < n_tiles; i++)
+    // both half-warps of a warp run the same number of groups (warp-uniform
+    // bound), so the full-mask shuffles below never diverge
+    const int ntok = max(0, te - t0);
+    const int per_hw = (ntok + ATT_HW - 1) / ATT_HW; // tokens of half-warp 0, the largest share
+    for (int i0 = 0; i0 < per_hw; i0 += ATT_UT)
     {
-        const int s = i % ATT_NST;
-        if (!mbar_wait_bounded(&bars[s], (i / ATT_NST) & 1, a.err, YLM_DEV_ERR_TIMEOUT_FULL))
-            ok = false;
-        if (ok)
+        uint4 kc_u[ATT_UT], vc_u[ATT_UT];
+#pragma unroll
+        for (int u = 0; u < ATT_UT; u++)
         {
-            const int nt = min(ATT_TT, te - (t0 + i * ATT_TT));
-            const __half *kt = reinterpret_cast<const __half *>(tiles + (size_t)s * 2 * TILE_BYTES);
-            const __half *vt = kt + ATT_TT * YLM_HEAD_DIM;
-            // both half-warps of a warp run the same trip count (warp-uniform
-            // bound) so the full-mask shuffles below never diverge
-            for (int kb = 2 * warp; kb < nt; kb += 8)
+            kc_u[u] = kr[u];
+            vc_u[u] = vr[u];
+        }
+        if (i0 + ATT_UT < per_hw)
+            load_group(i0 + ATT_UT);
+#pragma unroll
+        for (int u = 0; u < ATT_UT; u++)
+        {
+            const int t = t0 + hw + ATT_HW * (i0 + u);
+            const bool valid = t < te;
+            float kf[8], vf[8];
+            unpack8(kc_u[u], kf);
+            unpack8(vc_u[u], vf);
+#pragma unroll
+            for (int h = 0; h < G; h++)
             {
-                const int k = kb + (hw & 1);
-                const bool valid = k < nt;
-                float kf[8], vf[8];
-                const int kr = valid ? k : kb;
-                unpack8(*reinterpret_cast<const uint4 *>(kt + kr * YLM_HEAD_DIM + l16 * 8), kf);
-                unpack8(*reinterpret_cast<const uint4 *>(vt + kr * YLM_HEAD_DIM + l16 * 8), vf);
+                float sc = 0.f;
 #pragma unroll
-                for (int h = 0; h < G; h++)
-                {
-                    float sc = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 8; e++)
-                        sc = fmaf(q[h][e], kf[e], sc);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 8, 16);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 4, 16);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 2, 16);
-                    sc += __shfl_xor_sync(0xffffffffu, sc, 1, 16);
-                    if (valid)
-                        att_update(m[h], l[h], o[h], sc, vf);
-                }
+                for (int e = 0; e < 8; e++)
+                    sc = fmaf(q[h][e], kf[e], sc);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 8, 16);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 4, 16);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 2, 16);
+                sc += __shfl_xor_sync(0xffffffffu, sc, 1, 16);
+                if (valid)
+                    att_update(m[h], l[h], o[h], sc, vf);
             }
         }
-        __syncthreads();
-        if (!ok)
-            flags[0] = 1;
-        if (tid == 0 && ok && i + ATT_NST < n_tiles)
-            issue(i + ATT_NST);
-        __syncthreads();
-        if (flags[0])
-            break;
-    }
-    if (flags[0])
-    {
-        // drain copies still in flight, then leave without touching the counters
-        if (tid == 0)
-            for (int i = max(0, flags[2] - ATT_NST); i < flags[2]; i++)
-                mbar_wait_bounded(&bars[i % ATT_NST], (i / ATT_NST) & 1, a.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
-        return;
     }
     if (owns_new && hw == 0)
     {
@@ -266,7 +252,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
         }
     }
 
-    // ---- merge the 8 half-warps, then write this split's partial
+    // ---- merge the half-warps, then write this split's partial
 #pragma unroll
     for (int h = 0; h < G; h++)
     {
@@ -286,11 +272,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
     for (int h = 0; h < G; h++)
     {
         float M = -INFINITY;
-        for (int w = 0; w < 8; w++)
+        for (int w = 0; w < ATT_HW; w++)
             M = fmaxf(M, merge[(w * G + h) * ATT_ROW]);
         float L = 0.f, O = 0.f;
         if (M != -INFINITY)
-            for (int w = 0; w < 8; w++)
+            for (int w = 0; w < ATT_HW; w++)
             {
                 const float *row = merge + (w * G + h) * ATT_ROW;
                 const float c = exp2f(row[0] - M);
@@ -308,29 +294,41 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
     __threadfence();
     __syncthreads();
     if (tid == 0)
-        flags[1] = atomicAdd(&a.counters[g], 1);
+        ticket = atomicAdd(&a.counters[g], 1);
     __syncthreads();
-    if (flags[1] != S - 1)
+    if (ticket != S_eff - 1)
         return;
 
-    // ---- last CTA of this KV head: combine the splits
+    // ---- last CTA of this KV head: combine the splits. The (M, L) pairs are
+    // fetched in parallel into shared memory (the merge buffer is free now),
+    // then each thread sums its output dimension over the splits with the
+    // loads unrolled.
     __threadfence();
+    float *Ms = merge;                 // [G][S_eff]
+    float *Ls = merge + G * S_eff;     // [G][S_eff]
+    for (int i = tid; i < G * S_eff; i += ATT_THREADS)
+    {
+        const int h = i / S_eff, s = i % S_eff;
+        const float *pr = a.partial + ((size_t)(g * G + h) * S + s) * ATT_ROW;
+        Ms[i] = __ldcg(pr);
+        Ls[i] = __ldcg(pr + 1);
+    }
+    __syncthreads();
 #pragma unroll 1
     for (int h = 0; h < G; h++)
     {
-        const float *base = a.partial + (size_t)(g * G + h) * S * ATT_ROW;
         float M = -INFINITY;
-        for (int s = 0; s < S; s++)
-            M = fmaxf(M, __ldcg(base + s * ATT_ROW));
+        for (int s = 0; s < S_eff; s++)
+            M = fmaxf(M, Ms[h * S_eff + s]);
+        const float *base = a.partial + (size_t)(g * G + h) * S * ATT_ROW + 2 + d;
         float L = 0.f, O = 0.f;
-        for (int s = 0; s < S; s++)
+#pragma unroll 8
+        for (int s = 0; s < S_eff; s++)
         {
-            const float ms = __ldcg(base + s * ATT_ROW);
-            if (ms == -INFINITY)
-                continue;
-            const float c = exp2f(ms - M);
-            L += __ldcg(base + s * ATT_ROW + 1) * c;
-            O += __ldcg(base + s * ATT_ROW + 2 + d) * c;
+            const float ms = Ms[h * S_eff + s];
+            const float c = ms == -INFINITY ? 0.f : exp2f(ms - M);
+            L += Ls[h * S_eff + s] * c;
+            O += __ldcg(base + (size_t)s * ATT_ROW) * c;
         }
         a.out[(size_t)(g * G + h) * YLM_HEAD_DIM + d] = f2h(O / L);
     }
@@ -340,23 +338,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 
 size_t attn_partial_floats(int hq, int splits) { return (size_t)hq * splits * ATT_ROW; }
 
-int attn_default_splits(int hkv, int num_sms) { return std::max(1, num_sms / std::max(1, hkv)); }
-
-static size_t attn_smem_bytes(int G)
-{
-    size_t tiles = (size_t)ATT_NST * 2 * ATT_TT * YLM_HEAD_DIM * 2;
-    size_t merge = (size_t)8 * G * ATT_ROW * 4;
-    return std::max(tiles, merge) + (size_t)(G + 2) * YLM_HEAD_DIM * 4 + ATT_NST * 8 + 16;
-}
+// about two CTAs per SM over all KV heads
+int attn_default_splits(int hkv, int num_sms) { return std::max(1, 2 * num_sms / std::max(1, hkv)); }
 
 template <int G>
 static cudaError_t attn_launch_t(const AttnArgs &a, cudaStream_t s, bool pdl)
 {
-    const size_t smem = attn_smem_bytes(G);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.hkv, a.splits);
     cfg.blockDim = dim3(ATT_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -368,8 +359,8 @@ static cudaError_t attn_launch_t(const AttnArgs &a, cudaStream_t s, bool pdl)
 
 template <int G> static cudaError_t attn_prepare_t()
 {
-    return cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_smem_bytes(G));
+    return cudaFuncSetAttribute(attn_decode_kernel<G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
 }
 
 cudaError_t attn_prepare()

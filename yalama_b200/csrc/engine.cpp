@@ -755,7 +755,10 @@ struct ylm_engine
 
     void enqueue_forward(bool sample)
     {
+        // use_pdl: 1 every kernel may start early; 2 only the projections (the
+        // attention and the sampler wait for their producer to finish); 0 none
         const bool pdl = opt.use_pdl != 0;
+        const bool pdl_other = opt.use_pdl == 1;
         int *err = &dstate->err;
         for (int l = 0; l < L; l++)
         {
@@ -772,7 +775,7 @@ struct ylm_engine
             a.bias = y.bqkv;
             a.err = err;
             CK(gemv_launch(y.pq, l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, a, st, pdl));
-            CK(attn_decode_launch(attn_args(l), st, pdl));
+            CK(attn_decode_launch(attn_args(l), st, pdl_other));
             GemvArgs o;
             o.x = att;
             o.err = err;
@@ -821,7 +824,7 @@ struct ylm_engine
         if (tp > 1)
             NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
         if (sample)
-            CK(sample_launch(sample_args(), st, pdl));
+            CK(sample_launch(sample_args(), st, pdl_other));
     }
 
     cudaError_t resid_add_launch(__half *xx, const __half *y, int64_t n)
@@ -1181,7 +1184,7 @@ int ylm_options_default(ylm_engine_options *o)
     o->rope_compat = 1;
     o->rope_scaling = 0;
     o->use_cuda_graph = 1;
-    o->use_pdl = 1;
+    o->use_pdl = 0; // measured slower than plain graph launches on B200
     o->tp_size = 1;
     o->init_std = 0.02;
     o->zero_kv_on_begin = 1;

@@ -215,7 +215,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 else
                 {
-                    if (col0 + 32 <= p.N && !p.bias)
+                    // 16-byte stores only where the row start keeps them aligned (ldc % 8 == 0)
+                    if (col0 + 32 <= p.N && !p.bias && (p.ldc % 8) == 0 &&
+                        (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0)
                     {
                         uint4 pk[4];
                         __half2 *h = reinterpret_cast<__half2 *>(pk);

@@ -132,16 +132,35 @@ struct SelectShared
 // Threshold T (16-bit ordered value) such that fewer than k values exceed T and
 // at least k are >= T; also returns how many exceed it. `val(i)` gives the
 // ordered value of element i of this thread (valid(i) false -> ignored).
+// Add one to hist[bin] for every lane with valid == true; lanes that share a
+// bin are combined first (__match_any_sync), so clustered values (the top
+// logits often share a few FP16 bins) cost one shared atomic per distinct bin.
+__device__ __forceinline__ void hist_add(int *hist, uint32_t bin, bool valid)
+{
+    const int lane = threadIdx.x & 31;
+    const uint32_t key = valid ? bin : 0x10000u + (uint32_t)lane;
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    if (valid && lane == __ffs(peers) - 1)
+        atomicAdd(&hist[bin], __popc(peers));
+}
+
+// Threshold T (16-bit ordered value) such that fewer than k values exceed T and
+// at least k are >= T; also returns how many exceed it. `val(e)` gives the
+// ordered value of element e of this thread, e < n_mine; every thread loops to
+// n_max (block-uniform) so the warp-level aggregation stays convergent.
 template <typename ValF>
-__device__ __forceinline__ void radix_threshold(int k, int n_mine, ValF val, SelectShared &sh, uint32_t *T_out,
-                                                int *gt_out)
+__device__ __forceinline__ void radix_threshold(int k, int n_mine, int n_max, ValF val, SelectShared &sh,
+                                                uint32_t *T_out, int *gt_out)
 {
     const int tid = threadIdx.x;
     for (int b = tid; b < 256; b += SMP_THREADS)
         sh.hist[b] = 0;
     __syncthreads();
-    for (int e = 0; e < n_mine; e++)
-        atomicAdd(&sh.hist[val(e) >> 8], 1);
+    for (int e = 0; e < n_max; e++)
+    {
+        const bool ok = e < n_mine;
+        hist_add(sh.hist, ok ? (val(e) >> 8) : 0u, ok);
+    }
     __syncthreads();
     if (tid == 0)
     {
@@ -161,11 +180,11 @@ __device__ __forceinline__ void radix_threshold(int k, int n_mine, ValF val, Sel
     for (int b = tid; b < 256; b += SMP_THREADS)
         sh.hist[b] = 0;
     __syncthreads();
-    for (int e = 0; e < n_mine; e++)
+    for (int e = 0; e < n_max; e++)
     {
-        const uint32_t v = val(e);
-        if ((v >> 8) == B1)
-            atomicAdd(&sh.hist[v & 255], 1);
+        const bool ok = e < n_mine;
+        const uint32_t v = ok ? val(e) : 0u;
+        hist_add(sh.hist, v & 255, ok && (v >> 8) == B1);
     }
     __syncthreads();
     if (tid == 0)
@@ -261,7 +280,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const SampleArgs a)
         {
             uint32_t T;
             int gt;
-            radix_threshold(keff, n_mine, [&](int e) { return ov[e]; }, sh, &T, &gt);
+            radix_threshold(keff, n_mine, E, [&](int e) { return ov[e]; }, sh, &T, &gt);
             const int need = keff - gt;
             int n_eq = 0;
             for (int e = 0; e < n_mine; e++)
@@ -318,30 +337,57 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const SampleArgs a)
     }
     else
     {
-        // gather all candidate lists in part order (= vocabulary order)
+        // gather all candidate lists in part order (= vocabulary order): counts
+        // and offsets first, then every slot copied by its own thread
         uint64_t *all = reinterpret_cast<uint64_t *>(smem);
+        __shared__ int offs[SMP_THREADS + 1];
         int tot = 0;
-        int mycnt = 0;
         {
-            // parts are assigned to threads in contiguous runs so the scan keeps part order
-            const int ppt = (P + SMP_THREADS - 1) / SMP_THREADS;
+            const int ppt = (P + SMP_THREADS - 1) / SMP_THREADS; // parts per thread, contiguous runs
+            int mycnt = 0;
             for (int q = 0; q < ppt; q++)
             {
                 const int p = tid * ppt + q;
                 if (p < P)
                     mycnt += __ldcg(a.cand_count + p);
             }
-            int off = block_excl_scan(mycnt, sh.wsum, &tot);
+            const int off = block_excl_scan(mycnt, sh.wsum, &tot);
+            int o = off;
             for (int q = 0; q < ppt; q++)
             {
                 const int p = tid * ppt + q;
                 if (p < P)
                 {
-                    const int n = __ldcg(a.cand_count + p);
-                    for (int j = 0; j < n; j++)
-                        all[off + j] = __ldcg(reinterpret_cast<const unsigned long long *>(a.cand) + (size_t)p * SMP_KMAX + j);
-                    off += n;
+                    offs[p] = o;
+                    o += __ldcg(a.cand_count + p);
                 }
+            }
+            __syncthreads();
+            // eight independent loads in flight per thread, then the stores
+            for (int i0 = tid; i0 < P * SMP_KMAX; i0 += SMP_THREADS * 8)
+            {
+                unsigned long long v[8];
+                int dst[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                {
+                    const int i = i0 + u * SMP_THREADS;
+                    const int p = i / SMP_KMAX, j = i % SMP_KMAX;
+                    dst[u] = -1;
+                    if (i < P * SMP_KMAX)
+                    {
+                        const int cnt = (p + 1 < P ? offs[p + 1] : tot) - offs[p];
+                        if (j < cnt)
+                        {
+                            dst[u] = offs[p] + j;
+                            v[u] = __ldcg(reinterpret_cast<const unsigned long long *>(a.cand) + (size_t)p * SMP_KMAX + j);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    if (dst[u] >= 0)
+                        all[dst[u]] = v[u];
             }
         }
         __syncthreads();
@@ -351,7 +397,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const SampleArgs a)
         const int lo = min(M, tid * E2), hi = min(M, lo + E2);
         uint32_t T;
         int gt;
-        radix_threshold(keff, hi - lo, [&](int e) { return (uint32_t)(all[lo + e] >> 32); }, sh, &T, &gt);
+        radix_threshold(keff, hi - lo, E2, [&](int e) { return (uint32_t)(all[lo + e] >> 32); }, sh, &T, &gt);
         const int need = keff - gt;
         int n_eq = 0;
         for (int i = lo; i < hi; i++)
@@ -384,60 +430,74 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const SampleArgs a)
             sorted[rank] = k;
         }
         __syncthreads();
-        if (tid == 0)
+        // softmax over the sorted K values: exps in parallel (one lane per
+        // candidate), the sums sequentially in candidate order on lane 0 (the
+        // order the CPU restatement uses), then the inverse-CDF walk
+        __shared__ float ev[SMP_KMAX];
+        __shared__ float ssum;
+        if (warp == 0)
         {
-            float vals[SMP_KMAX], e[SMP_KMAX];
-            for (int i = 0; i < keff; i++)
-                vals[i] = __half2float(__ushort_as_half((unsigned short)unord16((uint32_t)(sorted[i] >> 32))));
-            float u;
-            if (st->u_override >= 0.f)
-                u = st->u_override;
-            else
+            for (int i = lane; i < keff; i += 32)
             {
-                const uint32_t x0 = philox_x0(st->seed, (uint64_t)st->sample_calls);
-                u = (float)(2u * (x0 >> 9) + 1u) * 5.9604644775390625e-08f;
+                const float v0 = __half2float(__ushort_as_half((unsigned short)unord16((uint32_t)(sorted[0] >> 32))));
+                const float vi = __half2float(__ushort_as_half((unsigned short)unord16((uint32_t)(sorted[i] >> 32))));
+                ev[i] = v0 == -INFINITY ? 0.f : exp_rn(__fsub_rn(vi, v0));
             }
-            int pick = 0;
-            if (keff > 0 && vals[0] != -INFINITY)
+            __syncwarp();
+            if (lane == 0)
             {
-                float s = 0.f;
+                float sacc = 0.f;
                 for (int i = 0; i < keff; i++)
+                    sacc = __fadd_rn(sacc, ev[i]);
+                ssum = sacc;
+            }
+            __syncwarp();
+            for (int i = lane; i < keff; i += 32)
+                ev[i] = ssum > 0.f ? __half2float(__float2half_rn(__fdiv_rn(ev[i], ssum))) : 0.f;
+            __syncwarp();
+            if (lane == 0)
+            {
+                float u;
+                if (st->u_override >= 0.f)
+                    u = st->u_override;
+                else
                 {
-                    e[i] = exp_rn(__fsub_rn(vals[i], vals[0]));
-                    s = __fadd_rn(s, e[i]);
+                    const uint32_t x0 = philox_x0(st->seed, (uint64_t)st->sample_calls);
+                    u = (float)(2u * (x0 >> 9) + 1u) * 5.9604644775390625e-08f;
                 }
-                float total = 0.f;
-                for (int i = 0; i < keff; i++)
+                int pick = 0;
+                if (keff > 0 && ssum > 0.f)
                 {
-                    e[i] = __half2float(__float2half_rn(__fdiv_rn(e[i], s)));
-                    total = __fadd_rn(total, e[i]);
-                }
-                const float target = __fmul_rn(u, total);
-                float cum = 0.f;
-                int last_pos = 0;
-                pick = -1;
-                for (int i = 0; i < keff; i++)
-                {
-                    if (e[i] > 0.f)
-                        last_pos = i;
-                    cum = __fadd_rn(cum, e[i]);
-                    if (cum > target)
-                    {
-                        pick = i;
-                        break;
-                    }
-                }
-                if (pick < 0)
-                    pick = last_pos;
-                if (a.dbg_ids)
+                    float total = 0.f;
+                    for (int i = 0; i < keff; i++)
+                        total = __fadd_rn(total, ev[i]);
+                    const float target = __fmul_rn(u, total);
+                    float cum = 0.f;
+                    int last_pos = 0;
+                    pick = -1;
                     for (int i = 0; i < keff; i++)
                     {
-                        a.dbg_ids[i] = key_idx(sorted[i]);
-                        a.dbg_probs[i] = e[i];
+                        if (ev[i] > 0.f)
+                            last_pos = i;
+                        cum = __fadd_rn(cum, ev[i]);
+                        if (cum > target)
+                        {
+                            pick = i;
+                            break;
+                        }
                     }
+                    if (pick < 0)
+                        pick = last_pos;
+                }
+                stw->u_used = u;
+                pick_key = keff > 0 ? sorted[pick] : 0;
             }
-            stw->u_used = u;
-            pick_key = keff > 0 ? sorted[pick] : 0;
+            if (a.dbg_ids)
+                for (int i = lane; i < keff; i += 32)
+                {
+                    a.dbg_ids[i] = key_idx(sorted[i]);
+                    a.dbg_probs[i] = ev[i];
+                }
         }
     }
     if (tid == 0)
@@ -464,13 +524,17 @@ int sample_parts(int64_t vocab, int num_sms)
 
 cudaError_t sample_prepare()
 {
-    return cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+    return e;
 }
 
 cudaError_t sample_launch(const SampleArgs &a, cudaStream_t s, bool pdl)
 {
     const int64_t chunk = (a.vocab + a.parts - 1) / a.parts;
-    if (chunk > SMP_THREADS * SMP_E)
+    if (chunk > SMP_THREADS * SMP_E || a.parts > SMP_THREADS)
         return cudaErrorInvalidValue;
     const size_t smem = (size_t)a.parts * SMP_KMAX * sizeof(uint64_t);
     if (smem > 160 * 1024)

@@ -56,20 +56,19 @@ enum GemvEpi
 
 struct GemvPlan
 {
-    CUtensorMap map;
     const __half *w;
-    int N, K;       // rows, columns of W
-    int rb;         // rows per block (TMA box height)
-    int n_blocks;   // ceil(N / rb)
-    int grid;       // CTAs
-    int nst;        // pipeline stages
-    int k_pad;      // K rounded up to 256
-    int pair;       // 1: SwiGLU row pairs
-    size_t smem;    // dynamic shared memory bytes
+    int N, K;    // rows, columns of W
+    int rb;      // rows per CTA (a contiguous range of W)
+    int grid;    // CTAs
+    int n_kc;    // 2048-column chunks per row
+    int k_pad;   // n_kc * 2048
+    int pair;    // 1: SwiGLU row pairs
+    size_t smem; // dynamic shared memory bytes
 };
 
 struct GemvArgs
 {
+    const __half *w = nullptr;      // set from the plan
     const __half *x = nullptr;      // input vector (PRO_VEC) or residual stream (PRO_RMSNORM)
     const __half *norm_w = nullptr; // RMSNorm weight [K]
     float eps = 0.f;
