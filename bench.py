@@ -125,6 +125,9 @@ def args_():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--e2e-requests", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small cases for profiler captures; not a bench number)")
+    ap.add_argument("--no-roofline", action="store_true")
     return ap.parse_args()
 
 
@@ -285,6 +288,9 @@ def bench_ours(a):
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     spec = synth.PRESETS[a.preset]
+    if a.layers:
+        import dataclasses
+        spec = dataclasses.replace(spec, layers=a.layers)
     cfg = E.config_from_spec(spec)
     eng = E.Engine(None, cfg, nccl_id=nccl_id, device=local, tp_rank=rank, tp_size=world,
                    init_seed=WORKLOAD["weight_seed"])
@@ -338,7 +344,7 @@ def bench_ours(a):
         if pg:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_tps.append((n - 1) / (float(t[0]) / 1e3))
-    e2e_v = statistics.median(e2e_tps)
+    e2e_v = statistics.median(e2e_tps) if e2e_tps else None
     # bytes crossing the host boundary per request: prompt in, 64-byte step state in/out per call
     calls = 2 + (a.decode - 1)
     h2d = a.prompt * 8 + 64 * calls
@@ -359,7 +365,7 @@ def bench_ours(a):
         if pg:
             pg.barrier()
         return
-    roof = gemv_roofline(spec, hbm, peak_kind) if world == 1 else None
+    roof = gemv_roofline(spec, hbm, peak_kind) if world == 1 and not a.no_roofline else None
     per_layer_kernels = 5 if world == 1 else 5
     launches_per_token = spec.layers * per_layer_kernels + 2
     prefill_launches = 1 + spec.layers * 8 + 1
@@ -368,7 +374,7 @@ def bench_ours(a):
             "warmup": a.warmup, "ms_per_step": (pf_ms + dec_ms) / a.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init N(0,0.02) weights, uniform-random prompt ids)",
-            "config": {"workload": f"{a.preset}-shaped FP16, batch 1, prompt {a.prompt}, {a.decode} generated tokens, "
+            "config": {"workload": f"{a.preset}-shaped FP16{f' ({a.layers} layers)' if a.layers else ''}, batch 1, prompt {a.prompt}, {a.decode} generated tokens, "
                                    f"top-k {WORKLOAD['top_k']}, temperature {WORKLOAD['temperature']}",
                        "parallelism": f"tp{world}", "l2": "weights 6.4 GB >> 126 MB L2 (no flush needed)",
                        "timing": "CUDA events on the engine stream; value = decode tokens / decode time"},
