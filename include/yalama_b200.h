@@ -177,6 +177,19 @@ int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, vo
 int ylm_k_decode_attention(const void *qkv, const void *q_norm, const void *k_norm, float eps, const void *rope_cos,
                            const void *rope_sin, int32_t max_pos, void *k_cache, void *v_cache, int32_t cap,
                            int32_t hq, int32_t hkv, int32_t slot, int32_t rope_pos, void *out, void *stream);
+/* The same decode-attention step with no device allocation, for callers that
+ * cannot allocate device memory (their memory is owned by their own pool, or an
+ * allocation's synchronisation is not acceptable where they call from). It has
+ * no counterpart in the reference. Scratch lives in one 2 MiB array that the
+ * library reserves on every GPU that loads it, for the life of the process:
+ * sizes needing more (hq x splits x 130 floats + KV-head tickets) return
+ * YLM_UNSUPPORTED. Calls share that array: calls that overlap on the GPU race,
+ * so serialise them. The first call on a device looks the array up (with that
+ * device current) and should come before any stream capture. */
+int ylm_k_decode_attention_noalloc(const void *qkv, const void *q_norm, const void *k_norm, float eps,
+                                   const void *rope_cos, const void *rope_sin, int32_t max_pos, void *k_cache,
+                                   void *v_cache, int32_t cap, int32_t hq, int32_t hkv, int32_t slot,
+                                   int32_t rope_pos, void *out, void *stream);
 /* Sample from FP16 logits on the device (greedy or top-k with uniform u). The
  * chosen id and, for top-k, the candidates and probabilities go to host memory. */
 int ylm_k_sample(const void *logits, int64_t vocab, int32_t greedy, int32_t top_k, float temperature,

@@ -145,6 +145,9 @@ SIGNATURES = {
     "ylm_k_decode_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, _P, _P]),
+    "ylm_k_decode_attention_noalloc": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
+                                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                      ctypes.c_int32, _P, _P]),
     "ylm_k_sample": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_float, _P,
                                     ctypes.c_float, _I64P, _I64P, _F32P, _P]),
 }
