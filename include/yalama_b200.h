@@ -90,6 +90,9 @@ typedef struct ylm_engine_options {
     double init_std;
     int32_t zero_kv_on_begin; /* 1 (default): BeginInfer zeroes the cache like ModelBase.cpp:302-309 */
     int32_t prefill_tensor_cores; /* 1 (default): tcgen05 GEMMs for prefill; 0: CUDA-core GEMMs */
+    int32_t decode_persistent;    /* 1: each decode step's forward is one cooperative kernel (single
+                                     GPU, up to 4 query heads per KV head; otherwise the per-op
+                                     graph); 0 (default): the per-op graph */
 } ylm_engine_options;
 
 /* ChatSession::Sample parameters (src/ChatSession.cpp:560-593). */
@@ -163,6 +166,10 @@ int ylm_last_prefill_ms(ylm_engine *e, double *ms);
 /* Time of one decode graph launch averaged over `iters` back-to-back launches
  * (CUDA events on the engine stream; state advanced on the device). */
 int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step);
+/* Which decode path the engine runs: *persistent = 1 when each decode step's
+ * forward is one cooperative kernel, 0 for the per-op graph. No counterpart in
+ * the reference (engine introspection for tests and benchmarks). */
+int ylm_decode_path(ylm_engine *e, int32_t *persistent);
 
 /* ---- kernel-level entry points (device pointers; stream = cudaStream_t or NULL) */
 /* y[n] = W[n,k] x[k], FP16 in and out, FP32 accumulation (the decode GEMV). */

@@ -45,7 +45,7 @@ int main(void) {
   printf("ylm_sampling %zu\n", sizeof(ylm_sampling));
   P(ylm_model_config, vocab_size) P(ylm_model_config, eos_ids) P(ylm_model_config, n_eos)
   P(ylm_engine_options, nccl_id) P(ylm_engine_options, init_seed) P(ylm_engine_options, zero_kv_on_begin)
-  P(ylm_engine_options, prefill_tensor_cores) P(ylm_engine_options, init_std)
+  P(ylm_engine_options, prefill_tensor_cores) P(ylm_engine_options, init_std) P(ylm_engine_options, decode_persistent)
   P(ylm_sampling, seed) P(ylm_sampling, masked_ids) P(ylm_sampling, n_masked)
   return 0;
 }

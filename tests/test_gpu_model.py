@@ -66,9 +66,10 @@ def run_teacher_forced(eng, orc, prompt, steps):
     return worst, mismatch
 
 
+@pytest.mark.parametrize("persistent", [0, 1])
 @pytest.mark.parametrize("fam", sorted(FAMILIES))
-def test_family_logits_match_oracle(fam):
-    spec, eng = make(FAMILIES[fam])
+def test_family_logits_match_oracle(fam, persistent):
+    spec, eng = make(FAMILIES[fam], decode_persistent=persistent)
     orc = OracleModel(spec, synth.model_weights(spec, 0), mode="f16", kv_gb=2)
     prompt = synth.prompt_ids(0, 24, spec.vocab)
     worst, _ = run_teacher_forced(eng, orc, prompt, 12)
@@ -97,8 +98,9 @@ def test_snapshot_load_equals_random_init(tmp_path):
 def test_graph_pdl_and_eager_agree():
     kw = FAMILIES["llama"]
     res = []
-    for opts in (dict(), dict(use_cuda_graph=0), dict(use_pdl=0), dict(use_cuda_graph=0, use_pdl=0)):
-        spec, eng = make(kw, **opts)
+    for opts in (dict(), dict(use_cuda_graph=0), dict(use_pdl=1), dict(use_cuda_graph=0, use_pdl=2)):
+        spec, eng = make(kw, decode_persistent=0, **opts)
+        assert not eng.decode_persistent()
         prompt = synth.prompt_ids(2, 20, spec.vocab)
         eng.begin_infer()
         eng.infer(prompt)
@@ -113,6 +115,66 @@ def test_graph_pdl_and_eager_agree():
         eng.close()
     for r in res[1:]:
         np.testing.assert_array_equal(res[0], r)
+
+
+def decode_rows(eng, prompt, steps):
+    """Logits of the prefill and of `steps` greedy decode steps."""
+    eng.begin_infer()
+    eng.infer(prompt)
+    lg = eng.logits()
+    rows, toks = [lg], []
+    for _ in range(steps):
+        tok = S.greedy(lg)
+        toks.append(tok)
+        eng.infer([tok])
+        lg = eng.logits()
+        rows.append(lg)
+    return np.stack(rows), toks
+
+
+# The persistent decode kernel computes the projections with the per-op
+# kernels' arithmetic order (bitwise equal); attention sums in another order,
+# so the logits agree to FP16 rounding of the attention output.
+PERSISTENT_TOL = 5e-3
+
+
+@pytest.mark.parametrize("fam", ["qwen3", "qwen2", "llama", "mistral"])
+def test_persistent_step_matches_per_op_graph(fam):
+    kw = FAMILIES[fam]
+    spec, ep = make(kw, decode_persistent=1)
+    _, eg = make(kw, decode_persistent=0)
+    assert ep.decode_persistent() and not eg.decode_persistent()
+    prompt = synth.prompt_ids(5, 40, spec.vocab)
+    rp, tp_ = decode_rows(ep, prompt, 16)
+    rg, tg = decode_rows(eg, prompt, 16)
+    np.testing.assert_array_equal(rp[0], rg[0])  # prefill path is shared
+    diff = float(np.max(np.abs(rp - rg)))
+    print(f"{fam}: persistent vs per-op max |logit diff| = {diff:.3e}")
+    assert diff < PERSISTENT_TOL
+    for i, (a, b) in enumerate(zip(tp_, tg)):
+        if a != b:
+            assert top2_gap(rg[i]) < TIE_GAP
+            break
+    ep.close()
+    eg.close()
+
+
+def test_persistent_long_context_and_fallback():
+    # a context of many splits per KV head, and the advance-mode decode loop
+    kw = FAMILIES["llama"]
+    spec, ep = make(kw, decode_persistent=1)
+    _, eg = make(kw, decode_persistent=0)
+    prompt = synth.prompt_ids(6, 1500, spec.vocab)
+    rp, _ = decode_rows(ep, prompt, 4)
+    rg, _ = decode_rows(eg, prompt, 4)
+    assert float(np.max(np.abs(rp - rg))) < PERSISTENT_TOL
+    assert ep.time_decode(8) > 0 and eg.time_decode(8) > 0
+    ep.close()
+    eg.close()
+    # more than 4 query heads per KV head: the per-op graph is used
+    _, e8 = make(FAMILIES["llama_g8"], decode_persistent=1)
+    assert not e8.decode_persistent()
+    e8.close()
 
 
 def test_kv_capacity_rule_matches_reference():
@@ -205,8 +267,9 @@ def test_topk_sampling_bit_exact_against_oracle():
         call += 1
 
 
-def test_generate_matches_oracle_greedy():
-    spec, eng = make(FAMILIES["llama"])
+@pytest.mark.parametrize("persistent", [0, 1])
+def test_generate_matches_oracle_greedy(persistent):
+    spec, eng = make(FAMILIES["llama"], decode_persistent=persistent)
     orc = OracleModel(spec, synth.model_weights(spec, 0), mode="f16")
     prompt = synth.prompt_ids(4, 32, spec.vocab)
     r = eng.generate(prompt, 24, eos_ids=[])

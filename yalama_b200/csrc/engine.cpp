@@ -292,6 +292,15 @@ struct ylm_engine
 
     cudaGraphExec_t g_fwd = nullptr, g_fwd_sample = nullptr;
 
+    // persistent decode step (decode_step.cu): phase table and barrier counters
+    bool ds_on = false;
+    int ds_G = 0;
+    size_t ds_smem = 0;
+    DsPhase *ds_ph = nullptr;
+    DsLayerAttn *ds_la = nullptr;
+    unsigned *ds_bar = nullptr, *ds_gen = nullptr;
+    DsArgs ds_args{};
+
     bool ready = false;
     int last = 0;
     int max_seq = 0;
@@ -331,7 +340,8 @@ struct ylm_engine
                         (void *)qkv, (void *)att, (void *)act, (void *)logits, (void *)logits_local, (void *)ar,
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
-                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds})
+                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_ph,
+                        (void *)ds_la, (void *)ds_bar, (void *)ds_gen})
             if (p)
                 cudaFree(p);
         wblob = nullptr;
@@ -407,6 +417,7 @@ struct ylm_engine
         alloc_kv();
         build_rope();
         alloc_workspace();
+        setup_persistent();
         compute_max_seq();
         CK(cudaStreamSynchronize(st));
     }
@@ -698,6 +709,121 @@ struct ylm_engine
         dbg_probs = dalloc<float>(64);
     }
 
+    // The persistent decode kernel: one cooperative launch per step, one CTA per
+    // SM. Used on a single GPU when a KV group has at most 4 query heads and
+    // the device can keep one CTA per SM resident; otherwise the per-op graph.
+    void setup_persistent()
+    {
+        ds_on = false;
+        if (!opt.decode_persistent || tp != 1)
+            return;
+        const int G = hq / hkv;
+        if (G < 1 || G > ds_max_heads_per_group())
+            return;
+        int coop = 0;
+        CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+        if (!coop)
+            return;
+        std::vector<DsPhase> ph;
+        std::vector<DsLayerAttn> la(L);
+        auto gemv = [&](int pro, int epi, int layer, const __half *w, int N, int K, const __half *in,
+                        const __half *nw, __half *out, const __half *bias, __half *resid) {
+            DsPhase p{};
+            p.kind = DS_GEMV;
+            p.pro = pro;
+            p.epi = epi;
+            p.layer = layer;
+            p.w = w;
+            p.N = N;
+            p.K = K;
+            p.x = in;
+            p.norm_w = nw;
+            p.out = out;
+            p.bias = bias;
+            p.resid = resid;
+            ph.push_back(p);
+        };
+        for (int l = 0; l < L; l++)
+        {
+            Layer &y = layers[l];
+            gemv(l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, l, y.wqkv, qkv_rows, H, x, y.ln1, qkv, y.bqkv, x);
+            DsPhase at{};
+            at.kind = DS_ATTN;
+            at.layer = l;
+            ph.push_back(at);
+            gemv(PRO_VEC, EPI_RESID, l, y.wo, H, hq * D, att, nullptr, nullptr, nullptr, x);
+            gemv(PRO_RMSNORM, EPI_SWIGLU, l, y.wgu, 2 * inter, H, x, y.ln2, act, nullptr, nullptr);
+            gemv(PRO_VEC, EPI_RESID, l, y.wd, H, inter, act, nullptr, nullptr, nullptr, x);
+            la[l].kc = kc + (size_t)l * kv_layer;
+            la[l].vc = vc + (size_t)l * kv_layer;
+            la[l].qn = y.qn;
+            la[l].kn = y.kn;
+            la[l].qkv = qkv;
+            la[l].out = att;
+        }
+        gemv(PRO_RMSNORM, EPI_STORE, -1, lm, (int)v_local, H, x, fnorm, logits_local, nullptr, nullptr);
+        const int C = sms;
+        const int kc_cols = ds_task_cols();
+        int kpad_max = 0, part_max = 0;
+        for (const DsPhase &p : ph)
+        {
+            if (p.kind != DS_GEMV)
+                continue;
+            const int nkc = (p.K + kc_cols - 1) / kc_cols;
+            kpad_max = std::max(kpad_max, nkc * kc_cols);
+            const int rows = p.epi == EPI_SWIGLU ? 2 * ((p.N / 2 + C - 1) / C) : (p.N + C - 1) / C;
+            part_max = std::max(part_max, rows * nkc);
+        }
+        const int nph = (int)ph.size();
+        const size_t tab_bytes = ((size_t)nph * 16 + 15) & ~(size_t)15;
+        const size_t gemv_bytes = (size_t)kpad_max * 2 + (size_t)part_max * 4 + 32 * 4;
+        const size_t work_bytes = (std::max(gemv_bytes, ds_attn_smem_bytes()) + 15) & ~(size_t)15;
+        const size_t xr_bytes = ((size_t)(H + C - 1) / C * 2 + 15) & ~(size_t)15;
+        const size_t smem = tab_bytes + work_bytes + xr_bytes;
+        if (smem > 220 * 1024)
+            return;
+        int bps = 0;
+        if (ds_prepare(G, smem, &bps) != cudaSuccess || bps < 1)
+        {
+            cudaGetLastError();
+            return;
+        }
+        ds_ph = dalloc<DsPhase>(nph);
+        ds_la = dalloc<DsLayerAttn>(L);
+        CK(cudaMemcpy(ds_ph, ph.data(), sizeof(DsPhase) * nph, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(ds_la, la.data(), sizeof(DsLayerAttn) * L, cudaMemcpyHostToDevice));
+        ds_bar = dalloc<unsigned>(nph);
+        ds_gen = dalloc<unsigned>(1);
+        DsArgs &d = ds_args;
+        d.ph = ds_ph;
+        d.nph = nph;
+        d.la = ds_la;
+        d.rope_cos = rcos;
+        d.rope_sin = rsin;
+        d.max_pos = max_pos;
+        d.cap = cap;
+        d.hq = hq;
+        d.hkv = hkv;
+        d.eps = cfg.rms_eps;
+        d.partial = partial;
+        d.counters = counters;
+        d.splits = splits;
+        d.emb = emb;
+        d.vocab = V;
+        d.state = dstate;
+        d.bar = ds_bar;
+        d.gen = ds_gen;
+        d.err = &dstate->err;
+        d.tab_bytes = (int)tab_bytes;
+        d.work_bytes = (int)work_bytes;
+        d.hidden = H;
+        d.kpad_max = kpad_max;
+        d.part_max = part_max;
+        ds_G = G;
+        ds_smem = smem;
+        ds_on = true;
+    }
+
     // ModelBase::CalculateMaxSequenceLength (ModelBase.cpp:312-338)
     void compute_max_seq()
     {
@@ -874,6 +1000,13 @@ struct ylm_engine
 
     void launch_forward(bool sample)
     {
+        if (ds_on)
+        {
+            CK(ds_launch(ds_args, ds_G, ds_smem, sms, st));
+            if (sample)
+                CK(sample_launch(sample_args(), st, false));
+            return;
+        }
         if (opt.use_cuda_graph)
         {
             cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
@@ -919,6 +1052,11 @@ struct ylm_engine
             // counters may be left mid-step: reset them so the next step starts clean
             cudaMemsetAsync(counters, 0, sizeof(int) * hkv, st);
             cudaMemsetAsync(smp_counter, 0, sizeof(int), st);
+            if (ds_bar)
+            {
+                cudaMemsetAsync(ds_bar, 0, sizeof(unsigned) * ds_args.nph, st);
+                cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
+            }
             cudaStreamSynchronize(st);
             if (e == YLM_DEV_ERR_BAD_TOKEN)
                 fail(YLM_INVALID_ARG, "token id out of range");
@@ -1189,6 +1327,7 @@ int ylm_options_default(ylm_engine_options *o)
     o->init_std = 0.02;
     o->zero_kv_on_begin = 1;
     o->prefill_tensor_cores = 1;
+    o->decode_persistent = 0;
     return YLM_OK;
 }
 
@@ -1550,6 +1689,14 @@ int ylm_last_prefill_ms(ylm_engine *e, double *ms)
     return YLM_OK;
 }
 
+int ylm_decode_path(ylm_engine *e, int32_t *persistent)
+{
+    if (!e || !persistent)
+        return YLM_INVALID_ARG;
+    *persistent = e->ds_on ? 1 : 0;
+    return YLM_OK;
+}
+
 int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
 {
     return guarded([&]() -> int {
@@ -1565,14 +1712,19 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
         e->fill_state(0, e->last + 1, e->opt.rope_compat ? e->last : e->last + 1, e->greedy != 0, 1);
         e->hin->token = e->hout->next_token >= 0 ? e->hout->next_token : 0;
         e->push_state();
-        if (!e->g_fwd_sample)
+        if (!e->ds_on && !e->g_fwd_sample)
             e->g_fwd_sample = e->capture(true);
         cudaEvent_t a, b;
         CK(cudaEventCreate(&a));
         CK(cudaEventCreate(&b));
         CK(cudaEventRecord(a, e->st));
         for (int i = 0; i < iters; i++)
-            CK(cudaGraphLaunch(e->g_fwd_sample, e->st));
+        {
+            if (e->ds_on)
+                e->launch_forward(true);
+            else
+                CK(cudaGraphLaunch(e->g_fwd_sample, e->st));
+        }
         CK(cudaEventRecord(b, e->st));
         CK(cudaEventSynchronize(b));
         float ms = 0;

@@ -88,6 +88,7 @@ class EngineOptions(ctypes.Structure):
         ("init_std", ctypes.c_double),
         ("zero_kv_on_begin", ctypes.c_int32),
         ("prefill_tensor_cores", ctypes.c_int32),
+        ("decode_persistent", ctypes.c_int32),
     ]
 
 
@@ -140,6 +141,7 @@ SIGNATURES = {
     "ylm_info": (ctypes.c_int, [_P, _I32P, _I32P, _I32P]),
     "ylm_time_decode": (ctypes.c_int, [_P, ctypes.c_int32, _F64P]),
     "ylm_last_prefill_ms": (ctypes.c_int, [_P, _F64P]),
+    "ylm_decode_path": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
     "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_decode_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
@@ -364,6 +366,12 @@ class Engine:
         st = lib().ylm_time_decode(self._h, iters, ctypes.byref(ms))
         check(st, "ylm_time_decode")
         return ms.value
+
+    def decode_persistent(self) -> bool:
+        """True when decode steps run as one cooperative kernel."""
+        v = ctypes.c_int32()
+        check(lib().ylm_decode_path(self._h, ctypes.byref(v)), "ylm_decode_path")
+        return bool(v.value)
 
 
 class Model:
