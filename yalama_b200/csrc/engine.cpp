@@ -292,14 +292,16 @@ struct ylm_engine
 
     cudaGraphExec_t g_fwd = nullptr, g_fwd_sample = nullptr;
 
-    // persistent decode step (decode_step.cu): phase table and barrier counters
+    // persistent GEMV segments (decode_step.cu): phase table, barrier counters,
+    // one argument block per segment (layer 0's QKV; O, gate-up, down and the
+    // next QKV per layer; the last ends with the lm_head)
     bool ds_on = false;
-    int ds_G = 0;
+    bool ds_graph_ok = true; // cleared if the cooperative launches cannot be captured
     size_t ds_smem = 0;
+    int ds_nph = 0;
     DsPhase *ds_ph = nullptr;
-    DsLayerAttn *ds_la = nullptr;
     unsigned *ds_bar = nullptr, *ds_gen = nullptr;
-    DsArgs ds_args{};
+    std::vector<DsArgs> ds_seg;
 
     bool ready = false;
     int last = 0;
@@ -341,7 +343,7 @@ struct ylm_engine
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
                         (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_ph,
-                        (void *)ds_la, (void *)ds_bar, (void *)ds_gen})
+                        (void *)ds_bar, (void *)ds_gen})
             if (p)
                 cudaFree(p);
         wblob = nullptr;
@@ -709,30 +711,25 @@ struct ylm_engine
         dbg_probs = dalloc<float>(64);
     }
 
-    // The persistent decode kernel: one cooperative launch per step, one CTA per
-    // SM. Used on a single GPU when a KV group has at most 4 query heads and
-    // the device can keep one CTA per SM resident; otherwise the per-op graph.
+    // Persistent GEMV segments: one cooperative launch (one CTA per SM) per run
+    // of projections between two attention launches. Single GPU only, and only
+    // where the device can keep one CTA per SM resident; otherwise the per-op
+    // graph.
     void setup_persistent()
     {
         ds_on = false;
         if (!opt.decode_persistent || tp != 1)
-            return;
-        const int G = hq / hkv;
-        if (G < 1 || G > ds_max_heads_per_group())
             return;
         int coop = 0;
         CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
         if (!coop)
             return;
         std::vector<DsPhase> ph;
-        std::vector<DsLayerAttn> la(L);
-        auto gemv = [&](int pro, int epi, int layer, const __half *w, int N, int K, const __half *in,
-                        const __half *nw, __half *out, const __half *bias, __half *resid) {
+        auto gemv = [&](int pro, int epi, const __half *w, int N, int K, const __half *in, const __half *nw,
+                        __half *out, const __half *bias, __half *resid) {
             DsPhase p{};
-            p.kind = DS_GEMV;
             p.pro = pro;
             p.epi = epi;
-            p.layer = layer;
             p.w = w;
             p.N = N;
             p.K = K;
@@ -743,32 +740,25 @@ struct ylm_engine
             p.resid = resid;
             ph.push_back(p);
         };
+        // phase order: QKV0 | O0 GU0 D0 QKV1 | ... | O(L-1) GU D lm_head
+        std::vector<int> cut; // segment boundaries
+        cut.push_back(0);
         for (int l = 0; l < L; l++)
         {
             Layer &y = layers[l];
-            gemv(l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, l, y.wqkv, qkv_rows, H, x, y.ln1, qkv, y.bqkv, x);
-            DsPhase at{};
-            at.kind = DS_ATTN;
-            at.layer = l;
-            ph.push_back(at);
-            gemv(PRO_VEC, EPI_RESID, l, y.wo, H, hq * D, att, nullptr, nullptr, nullptr, x);
-            gemv(PRO_RMSNORM, EPI_SWIGLU, l, y.wgu, 2 * inter, H, x, y.ln2, act, nullptr, nullptr);
-            gemv(PRO_VEC, EPI_RESID, l, y.wd, H, inter, act, nullptr, nullptr, nullptr, x);
-            la[l].kc = kc + (size_t)l * kv_layer;
-            la[l].vc = vc + (size_t)l * kv_layer;
-            la[l].qn = y.qn;
-            la[l].kn = y.kn;
-            la[l].qkv = qkv;
-            la[l].out = att;
+            gemv(l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, y.wqkv, qkv_rows, H, x, y.ln1, qkv, y.bqkv, x);
+            cut.push_back((int)ph.size()); // attention of layer l runs here
+            gemv(PRO_VEC, EPI_RESID, y.wo, H, hq * D, att, nullptr, nullptr, nullptr, x);
+            gemv(PRO_RMSNORM, EPI_SWIGLU, y.wgu, 2 * inter, H, x, y.ln2, act, nullptr, nullptr);
+            gemv(PRO_VEC, EPI_RESID, y.wd, H, inter, act, nullptr, nullptr, nullptr, x);
         }
-        gemv(PRO_RMSNORM, EPI_STORE, -1, lm, (int)v_local, H, x, fnorm, logits_local, nullptr, nullptr);
+        gemv(PRO_RMSNORM, EPI_STORE, lm, (int)v_local, H, x, fnorm, logits_local, nullptr, nullptr);
+        cut.push_back((int)ph.size());
         const int C = sms;
         const int kc_cols = ds_task_cols();
         int kpad_max = 0, part_max = 0;
         for (const DsPhase &p : ph)
         {
-            if (p.kind != DS_GEMV)
-                continue;
             const int nkc = (p.K + kc_cols - 1) / kc_cols;
             kpad_max = std::max(kpad_max, nkc * kc_cols);
             const int rows = p.epi == EPI_SWIGLU ? 2 * ((p.N / 2 + C - 1) / C) : (p.N + C - 1) / C;
@@ -776,50 +766,45 @@ struct ylm_engine
         }
         const int nph = (int)ph.size();
         const size_t tab_bytes = ((size_t)nph * 16 + 15) & ~(size_t)15;
-        const size_t gemv_bytes = (size_t)kpad_max * 2 + (size_t)part_max * 4 + 32 * 4;
-        const size_t work_bytes = (std::max(gemv_bytes, ds_attn_smem_bytes()) + 15) & ~(size_t)15;
+        const size_t work_bytes = ((size_t)kpad_max * 2 + (size_t)part_max * 4 + 32 * 4 + 15) & ~(size_t)15;
         const size_t xr_bytes = ((size_t)(H + C - 1) / C * 2 + 15) & ~(size_t)15;
         const size_t smem = tab_bytes + work_bytes + xr_bytes;
         if (smem > 220 * 1024)
             return;
         int bps = 0;
-        if (ds_prepare(G, smem, &bps) != cudaSuccess || bps < 1)
+        if (ds_prepare(smem, &bps) != cudaSuccess || bps < 1)
         {
             cudaGetLastError();
             return;
         }
         ds_ph = dalloc<DsPhase>(nph);
-        ds_la = dalloc<DsLayerAttn>(L);
         CK(cudaMemcpy(ds_ph, ph.data(), sizeof(DsPhase) * nph, cudaMemcpyHostToDevice));
-        CK(cudaMemcpy(ds_la, la.data(), sizeof(DsLayerAttn) * L, cudaMemcpyHostToDevice));
         ds_bar = dalloc<unsigned>(nph);
         ds_gen = dalloc<unsigned>(1);
-        DsArgs &d = ds_args;
+        DsArgs d{};
         d.ph = ds_ph;
-        d.nph = nph;
-        d.la = ds_la;
-        d.rope_cos = rcos;
-        d.rope_sin = rsin;
-        d.max_pos = max_pos;
-        d.cap = cap;
-        d.hq = hq;
-        d.hkv = hkv;
         d.eps = cfg.rms_eps;
-        d.partial = partial;
-        d.counters = counters;
-        d.splits = splits;
         d.emb = emb;
         d.vocab = V;
         d.state = dstate;
+        d.x = x;
+        d.hidden = H;
         d.bar = ds_bar;
         d.gen = ds_gen;
         d.err = &dstate->err;
         d.tab_bytes = (int)tab_bytes;
         d.work_bytes = (int)work_bytes;
-        d.hidden = H;
         d.kpad_max = kpad_max;
         d.part_max = part_max;
-        ds_G = G;
+        ds_seg.clear();
+        for (size_t k = 0; k + 1 < cut.size(); k++)
+        {
+            d.p0 = cut[k];
+            d.p1 = cut[k + 1];
+            d.last = k + 2 == cut.size() ? 1 : 0;
+            ds_seg.push_back(d);
+        }
+        ds_nph = nph;
         ds_smem = smem;
         ds_on = true;
     }
@@ -881,6 +866,19 @@ struct ylm_engine
 
     void enqueue_forward(bool sample)
     {
+        if (ds_on)
+        {
+            // segment 0 (layer 0's QKV), then attention l and segment l + 1
+            for (int l = 0; l <= L; l++)
+            {
+                CK(ds_launch(ds_seg[l], ds_smem, sms, st));
+                if (l < L)
+                    CK(attn_decode_launch(attn_args(l), st, false));
+            }
+            if (sample)
+                CK(sample_launch(sample_args(), st, false));
+            return;
+        }
         // use_pdl: 1 every kernel may start early; 2 only the projections (the
         // attention and the sampler wait for their producer to finish); 0 none
         const bool pdl = opt.use_pdl != 0;
@@ -1000,11 +998,32 @@ struct ylm_engine
 
     void launch_forward(bool sample)
     {
+        if (ds_on && opt.use_cuda_graph && ds_graph_ok)
+        {
+            cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
+            if (!ex)
+            {
+                try
+                {
+                    ex = capture(sample);
+                }
+                catch (...)
+                {
+                    // cooperative launches that do not capture: launch them directly
+                    ds_graph_ok = false;
+                    ex = nullptr;
+                    cudaGetLastError();
+                }
+            }
+            if (ex)
+            {
+                CK(cudaGraphLaunch(ex, st));
+                return;
+            }
+        }
         if (ds_on)
         {
-            CK(ds_launch(ds_args, ds_G, ds_smem, sms, st));
-            if (sample)
-                CK(sample_launch(sample_args(), st, false));
+            enqueue_forward(sample);
             return;
         }
         if (opt.use_cuda_graph)
@@ -1054,7 +1073,7 @@ struct ylm_engine
             cudaMemsetAsync(smp_counter, 0, sizeof(int), st);
             if (ds_bar)
             {
-                cudaMemsetAsync(ds_bar, 0, sizeof(unsigned) * ds_args.nph, st);
+                cudaMemsetAsync(ds_bar, 0, sizeof(unsigned) * ds_nph, st);
                 cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
             }
             cudaStreamSynchronize(st);
@@ -1712,19 +1731,27 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
         e->fill_state(0, e->last + 1, e->opt.rope_compat ? e->last : e->last + 1, e->greedy != 0, 1);
         e->hin->token = e->hout->next_token >= 0 ? e->hout->next_token : 0;
         e->push_state();
-        if (!e->ds_on && !e->g_fwd_sample)
-            e->g_fwd_sample = e->capture(true);
+        // the first launch captures the graph (outside the timed region)
+        if (!e->g_fwd_sample && e->opt.use_cuda_graph && (!e->ds_on || e->ds_graph_ok))
+        {
+            e->launch_forward(true);
+            CK(cudaStreamSynchronize(e->st));
+            e->pull_state_sync();
+            e->last += 1;
+            e->calls += 1;
+            iters -= 1;
+            if (iters <= 0)
+            {
+                *ms_per_step = 0.0;
+                return YLM_OK;
+            }
+        }
         cudaEvent_t a, b;
         CK(cudaEventCreate(&a));
         CK(cudaEventCreate(&b));
         CK(cudaEventRecord(a, e->st));
         for (int i = 0; i < iters; i++)
-        {
-            if (e->ds_on)
-                e->launch_forward(true);
-            else
-                CK(cudaGraphLaunch(e->g_fwd_sample, e->st));
-        }
+            e->launch_forward(true);
         CK(cudaEventRecord(b, e->st));
         CK(cudaEventSynchronize(b));
         float ms = 0;

@@ -131,19 +131,13 @@ int sample_parts(int64_t vocab, int num_sms);
 cudaError_t sample_launch(const SampleArgs &a, cudaStream_t s, bool pdl);
 cudaError_t sample_prepare();
 
-// ------------------------------------------------------------------ persistent decode step
-// One cooperative launch runs the whole per-token forward (decode_step.cu).
-enum DsKind
-{
-    DS_GEMV = 0,
-    DS_ATTN = 1
-};
+// ------------------------------------------------------------------ persistent GEMV segments
+// The projections between two attention launches of a decode step run as one
+// cooperative launch (decode_step.cu).
 struct DsPhase
 {
-    int kind;  // DS_GEMV / DS_ATTN
-    int pro;   // GemvPro
-    int epi;   // GemvEpi
-    int layer; // DS_ATTN: layer index into DsArgs::la
+    int pro;         // GemvPro
+    int epi;         // GemvEpi
     const __half *w; // [N, K] row-major
     int N, K;
     const __half *x;      // PRO_VEC input, or the residual stream for the RMSNorm prologues
@@ -153,44 +147,30 @@ struct DsPhase
     __half *resid;        // EPI_RESID target; PRO_EMBED_RMSNORM: each CTA writes its residual rows of
                           // the embedding row here
 };
-struct DsLayerAttn
-{
-    __half *kc, *vc;          // this layer's cache, [hkv][cap][128]
-    const __half *qn, *kn;    // per-head RMSNorm weights or null
-    const __half *qkv;        // QKV projection output
-    __half *out;              // attention output [hq * 128]
-};
 struct DsArgs
 {
-    const DsPhase *ph; // [nph], device memory
-    int nph;
-    const DsLayerAttn *la; // [layers], device memory
-    const __half *rope_cos, *rope_sin;
-    int max_pos, cap, hq, hkv;
+    const DsPhase *ph; // the step's GEMV phases, device memory
+    int p0, p1;        // this launch runs phases [p0, p1)
+    int last;          // 1: the step's last segment (advances *gen)
     float eps;
-    float *partial; // attention partials [hq][splits][130]
-    int *counters;  // [hkv] attention tickets, zero between launches
-    int splits;     // splits the partial buffer holds per head
     const __half *emb;
     int64_t vocab;
-    StepState *state;
-    unsigned *bar; // [nph] arrival counters, monotonic across launches
-    unsigned *gen; // launches completed
+    const StepState *state;
+    const __half *x;   // residual stream [hidden]
+    int hidden;        // each CTA keeps its rows of it (split like an N = hidden projection)
+    unsigned *bar;     // [phases] arrival counters, monotonic across steps
+    unsigned *gen;     // decode steps completed
     int *err;
     int tab_bytes;  // shared-memory layout: phase table, work area, residual rows
-    int work_bytes; // the work area (GEMV input and partials, or attention scratch)
-    int kpad_max;   // largest input vector (halves, multiple of 2048)
+    int work_bytes; // GEMV input vector, partials, RMSNorm scratch
+    int kpad_max;   // largest input vector (halves, multiple of the task width)
     int part_max;   // largest per-CTA task count of a phase
-    int hidden;     // residual stream length H; each CTA keeps its rows of it
-                    // (split like an N = H projection) after the work area
 };
-size_t ds_attn_smem_bytes();
-int ds_max_heads_per_group();
 int ds_threads();
 int ds_task_cols();
-// Shared-memory opt-in for heads-per-group G and the resulting CTAs per SM.
-cudaError_t ds_prepare(int G, size_t smem, int *blocks_per_sm);
-cudaError_t ds_launch(const DsArgs &a, int G, size_t smem, int grid, cudaStream_t s);
+// Shared-memory opt-in and the resulting CTAs per SM.
+cudaError_t ds_prepare(size_t smem, int *blocks_per_sm);
+cudaError_t ds_launch(const DsArgs &a, size_t smem, int grid, cudaStream_t s);
 
 // Shared-memory opt-in of every kernel on the current device (idempotent).
 cudaError_t kernels_prepare();
