@@ -19,6 +19,7 @@
 #include "ylm_common.cuh"
 #include "ylm_kernels.h"
 #include <algorithm>
+#include <cooperative_groups.h>
 
 namespace ylm {
 
@@ -336,6 +337,311 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
         a.counters[g] = 0;
 }
 
+// ---------------------------------------------------------------- cluster variant
+// One thread-block cluster per KV head, one CTA per split of the cached
+// tokens (S = cluster size, 16 where the device allows non-portable clusters,
+// else 8). Inside a CTA each warp takes whole tokens (lane l holds dimensions
+// 4l..4l+3), ATC_UT tokens per batch: all their scores first, then one
+// rescale of the running softmax state. The 8 warp states are merged in
+// shared memory; each CTA then stores its partial (M, L and one slice of O per
+// head) into the shared memory of the rank that owns that slice (distributed
+// shared memory), and after one cluster barrier every rank combines its slice
+// of the S partials and writes it. No global scratch, fence or atomic ticket.
+constexpr int ATC_THREADS = 256;
+constexpr int ATC_WARPS = ATC_THREADS / 32;
+constexpr int ATC_MAX_SPLITS = 16; // largest cluster
+constexpr int ATC_MIN_SPLITS = 8;  // smallest cluster (the portable size)
+
+static int g_cluster_splits = 0; // 16, 8, or 0 (no cluster launch: split-K kernel)
+
+template <int G>
+__global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArgs a)
+{
+    constexpr int UT = G <= 4 ? 8 : 4; // tokens per warp batch
+    __shared__ float q_s[G * YLM_HEAD_DIM];
+    __shared__ float kn_s[YLM_HEAD_DIM], vn_s[YLM_HEAD_DIM];
+    __shared__ float mrg[ATC_WARPS * G * ATT_ROW];
+    __shared__ float recv[ATC_MAX_SPLITS * G * (2 + YLM_HEAD_DIM / ATC_MIN_SPLITS)]; // [rank][head][M, L, slice]
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    const int S = (int)cl.num_blocks();
+    const int sp = (int)cl.block_rank();
+    const int g = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // every CTA of the cluster must have started before another one writes
+    // into its shared memory: arrive now, wait before the first remote store
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    pdl_launch_dependents();
+    const int slot = a.state->slot;
+    const int pos = a.state->rope_pos;
+    const bool ok = slot >= 0 && slot < a.cap && pos >= 0 && pos < a.max_pos;
+    if (!ok && sp == 0 && g == 0 && tid == 0 && a.err)
+        atomicExch(a.err, YLM_DEV_ERR_BAD_STATE);
+    const int n = ok ? slot + 1 : 0;
+    const int chunk = (n + S - 1) / S;
+    const int t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk);
+    const bool owns_new = ok && slot >= t0 && slot < t1;
+    const int te = owns_new ? slot : t1; // cached tokens [t0, te); the new one comes from qkv
+    const __half *kc = a.k_cache + (size_t)g * a.cap * YLM_HEAD_DIM + lane * 4;
+    const __half *vc = a.v_cache + (size_t)g * a.cap * YLM_HEAD_DIM + lane * 4;
+
+    // token j of this warp: t0 + warp + 8 j; earlier slots are constant during
+    // the step, so the first batch is loaded before griddepcontrol.wait
+    uint2 kr[UT], vr[UT];
+    auto load_batch = [&](int j0) {
+#pragma unroll
+        for (int u = 0; u < UT; u++)
+        {
+            const int t = t0 + warp + ATC_WARPS * (j0 + u);
+            if (t < te)
+            {
+                kr[u] = __ldg(reinterpret_cast<const uint2 *>(kc + (size_t)t * YLM_HEAD_DIM));
+                vr[u] = __ldg(reinterpret_cast<const uint2 *>(vc + (size_t)t * YLM_HEAD_DIM));
+            }
+        }
+    };
+    load_batch(0);
+    pdl_wait();
+
+    if (ok)
+    {
+        const __half *cosr = a.rope_cos + (size_t)pos * 64;
+        const __half *sinr = a.rope_sin + (size_t)pos * 64;
+        for (int h = warp; h < G + 2; h += ATC_WARPS)
+        {
+            if (h < G)
+                prep_head(a.qkv + (size_t)(g * G + h) * YLM_HEAD_DIM, a.q_norm, a.eps, cosr, sinr, true,
+                          q_s + h * YLM_HEAD_DIM, lane);
+            else if (h == G && owns_new)
+            {
+                prep_head(a.qkv + (size_t)(a.hq + g) * YLM_HEAD_DIM, a.k_norm, a.eps, cosr, sinr, true, kn_s, lane);
+                __syncwarp();
+                for (int d = lane; d < YLM_HEAD_DIM; d += 32)
+                    a.k_cache[((size_t)g * a.cap + slot) * YLM_HEAD_DIM + d] = f2h(kn_s[d]);
+            }
+            else if (h == G + 1 && owns_new)
+                for (int d = lane; d < YLM_HEAD_DIM; d += 32)
+                {
+                    const __half v = a.qkv[(size_t)(a.hq + a.hkv + g) * YLM_HEAD_DIM + d];
+                    vn_s[d] = h2f(v);
+                    a.v_cache[((size_t)g * a.cap + slot) * YLM_HEAD_DIM + d] = v;
+                }
+        }
+    }
+    __syncthreads();
+
+    float q[G][4], o[G][4], m[G], l[G];
+#pragma unroll
+    for (int h = 0; h < G; h++)
+    {
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+        {
+            q[h][e] = q_s[h * YLM_HEAD_DIM + lane * 4 + e] * ATT_SCALE_LOG2;
+            o[h][e] = 0.f;
+        }
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+    }
+    const int ntok = max(0, te - t0 - warp);
+    const int per_w = (ntok + ATC_WARPS - 1) / ATC_WARPS; // this warp's cached tokens
+    for (int j0 = 0; j0 < per_w; j0 += UT)
+    {
+        uint2 kcur[UT], vcur[UT];
+#pragma unroll
+        for (int u = 0; u < UT; u++)
+        {
+            kcur[u] = kr[u];
+            vcur[u] = vr[u];
+        }
+        if (j0 + UT < per_w)
+            load_batch(j0 + UT);
+        float sc[UT][G];
+#pragma unroll
+        for (int u = 0; u < UT; u++)
+        {
+            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kcur[u]);
+            const float2 ka = __half22float2(k2[0]), kb = __half22float2(k2[1]);
+#pragma unroll
+            for (int h = 0; h < G; h++)
+                sc[u][h] = fmaf(q[h][3], kb.y, fmaf(q[h][2], kb.x, fmaf(q[h][1], ka.y, q[h][0] * ka.x)));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < UT; u++)
+#pragma unroll
+                for (int h = 0; h < G; h++)
+                    sc[u][h] += __shfl_xor_sync(0xffffffffu, sc[u][h], off);
+#pragma unroll
+        for (int h = 0; h < G; h++)
+        {
+            float mx = m[h];
+#pragma unroll
+            for (int u = 0; u < UT; u++)
+                if (j0 + u < per_w)
+                    mx = fmaxf(mx, sc[u][h]);
+            const float cs = exp2f(m[h] - mx);
+            l[h] *= cs;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                o[h][e] *= cs;
+#pragma unroll
+            for (int u = 0; u < UT; u++)
+                if (j0 + u < per_w)
+                {
+                    const float ps = exp2f(sc[u][h] - mx);
+                    const __half2 *v2 = reinterpret_cast<const __half2 *>(&vcur[u]);
+                    const float2 va = __half22float2(v2[0]), vb = __half22float2(v2[1]);
+                    l[h] += ps;
+                    o[h][0] += ps * va.x;
+                    o[h][1] += ps * va.y;
+                    o[h][2] += ps * vb.x;
+                    o[h][3] += ps * vb.y;
+                }
+            m[h] = mx;
+        }
+    }
+    if (owns_new && warp == 0)
+    {
+        // the new token, from shared memory
+#pragma unroll
+        for (int h = 0; h < G; h++)
+        {
+            float sc = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                sc = fmaf(q[h][e], kn_s[lane * 4 + e], sc);
+            sc = warp_sum(sc);
+            const float mn = fmaxf(m[h], sc);
+            const float cs = exp2f(m[h] - mn);
+            const float ps = exp2f(sc - mn);
+            l[h] = l[h] * cs + ps;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                o[h][e] = o[h][e] * cs + ps * vn_s[lane * 4 + e];
+            m[h] = mn;
+        }
+    }
+    // warp states -> this CTA's partial (M, L, O per head)
+#pragma unroll
+    for (int h = 0; h < G; h++)
+    {
+        float *row = mrg + (warp * G + h) * ATT_ROW;
+        if (lane == 0)
+        {
+            row[0] = m[h];
+            row[1] = l[h];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            row[2 + lane * 4 + e] = o[h][e];
+    }
+    __syncthreads();
+    // this CTA's partial, pushed straight into the cluster: rank q combines
+    // dimensions [q * slice, (q + 1) * slice) of every head, so it receives
+    // every rank's (M, L) and that slice of every rank's O (remote stores,
+    // no round trips); one cluster barrier then publishes them
+    const int slice = YLM_HEAD_DIM / S;
+    const int RW = 2 + slice;
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    for (int k = tid; k < G * YLM_HEAD_DIM; k += ATC_THREADS)
+    {
+        const int h = k >> 7, d = k & 127;
+        float M = -INFINITY;
+        for (int w = 0; w < ATC_WARPS; w++)
+            M = fmaxf(M, mrg[(w * G + h) * ATT_ROW]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY)
+            for (int w = 0; w < ATC_WARPS; w++)
+            {
+                const float *row = mrg + (w * G + h) * ATT_ROW;
+                const float c = exp2f(row[0] - M);
+                L += row[1] * c;
+                O += row[2 + d] * c;
+            }
+        const int qd = d / slice;
+        float *dst = cl.map_shared_rank(recv, qd) + (sp * G + h) * RW;
+        dst[2 + d - qd * slice] = O;
+        if (d - qd * slice == 0)
+        {
+            dst[0] = M;
+            dst[1] = L;
+        }
+    }
+    cl.sync(); // every rank's slices have landed
+    if (ok)
+        for (int k = tid; k < G * slice; k += ATC_THREADS)
+        {
+            const int h = k / slice, dl = k - h * slice;
+            float M = -INFINITY;
+            for (int r = 0; r < S; r++)
+                M = fmaxf(M, recv[(r * G + h) * RW]);
+            float L = 0.f, O = 0.f;
+            for (int r = 0; r < S; r++)
+            {
+                const float *row = recv + (r * G + h) * RW;
+                const float c = row[0] == -INFINITY ? 0.f : exp2f(row[0] - M);
+                L += row[1] * c;
+                O += row[2 + dl] * c;
+            }
+            a.out[(size_t)(g * G + h) * YLM_HEAD_DIM + sp * slice + dl] = f2h(O / L);
+        }
+}
+
+template <int G>
+static cudaError_t attn_cluster_launch_t(const AttnArgs &a, int S, cudaStream_t s, bool pdl)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, a.hkv);
+    cfg.blockDim = dim3(ATC_THREADS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = S;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    na++;
+    if (pdl)
+    {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<G>, a);
+}
+
+// Largest cluster size (16, else 8) that the device can schedule for G, or 0.
+template <int G> static int attn_cluster_prepare_t()
+{
+    if (cudaFuncSetAttribute(attn_cluster_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+        cudaSuccess)
+        cudaGetLastError();
+    for (int S : {16, 8})
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, 1);
+        cfg.blockDim = dim3(ATC_THREADS);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = S;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int nc = 0;
+        if (cudaOccupancyMaxActiveClusters(&nc, attn_cluster_kernel<G>, &cfg) == cudaSuccess && nc >= 1)
+            return S;
+        cudaGetLastError();
+    }
+    return 0;
+}
+
 size_t attn_partial_floats(int hq, int splits) { return (size_t)hq * splits * ATT_ROW; }
 
 // about two CTAs per SM over all KV heads
@@ -365,6 +671,16 @@ template <int G> static cudaError_t attn_prepare_t()
 
 cudaError_t attn_prepare()
 {
+    int S = 16;
+    S = std::min(S, attn_cluster_prepare_t<1>());
+    S = std::min(S, attn_cluster_prepare_t<2>());
+    S = std::min(S, attn_cluster_prepare_t<3>());
+    S = std::min(S, attn_cluster_prepare_t<4>());
+    S = std::min(S, attn_cluster_prepare_t<5>());
+    S = std::min(S, attn_cluster_prepare_t<6>());
+    S = std::min(S, attn_cluster_prepare_t<7>());
+    S = std::min(S, attn_cluster_prepare_t<8>());
+    g_cluster_splits = S;
     cudaError_t e = cudaSuccess;
     if (e == cudaSuccess) e = attn_prepare_t<1>();
     if (e == cudaSuccess) e = attn_prepare_t<2>();
@@ -381,6 +697,20 @@ cudaError_t attn_decode_launch(const AttnArgs &a, cudaStream_t s, bool pdl)
 {
     if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.splits <= 0)
         return cudaErrorInvalidValue;
+    const int S = g_cluster_splits;
+    if (S > 0)
+        switch (a.hq / a.hkv)
+        {
+        case 1: return attn_cluster_launch_t<1>(a, S, s, pdl);
+        case 2: return attn_cluster_launch_t<2>(a, S, s, pdl);
+        case 3: return attn_cluster_launch_t<3>(a, S, s, pdl);
+        case 4: return attn_cluster_launch_t<4>(a, S, s, pdl);
+        case 5: return attn_cluster_launch_t<5>(a, S, s, pdl);
+        case 6: return attn_cluster_launch_t<6>(a, S, s, pdl);
+        case 7: return attn_cluster_launch_t<7>(a, S, s, pdl);
+        case 8: return attn_cluster_launch_t<8>(a, S, s, pdl);
+        default: return cudaErrorInvalidValue;
+        }
     switch (a.hq / a.hkv)
     {
     case 1: return attn_launch_t<1>(a, s, pdl);
