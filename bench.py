@@ -254,6 +254,20 @@ def gemv_roofline(spec, hbm_peak, peak_kind):
             "avg_launch_us": ms * 1e3}
 
 
+def segment_roofline(eng, spec, hbm_peak, peak_kind):
+    """The dominant kernel of the persistent path: one decode GEMV segment (a
+    middle layer's O, gate-up, down and the next layer's QKV, one cooperative
+    launch) timed alone with CUDA events on the engine stream, back to back;
+    its weights (201 MB for the 3B shape) exceed L2, so every launch streams
+    them from HBM. Algorithmic bytes = the segment's weights."""
+    ms, wbytes = eng.time_segment(spec.layers // 2, 48)
+    achieved = wbytes / (ms * 1e-3) / 1e9
+    return {"kernel": "decode_segment_kernel (O + gate-up + down + next QKV of one layer, FP16)",
+            "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+            "peak_kind": peak_kind, "traffic": profile_traffic("decode_segment_llama3.2-3b.txt"),
+            "algorithmic_bytes": wbytes, "avg_launch_us": ms * 1e3}
+
+
 def decode_bytes_per_token(spec, ctx, tp):
     """Weights + KV read per decode token per GPU (algorithmic)."""
     H, D, I, V = spec.hidden, spec.head_dim, spec.intermediate, spec.vocab
@@ -354,6 +368,10 @@ def bench_ours(a):
     ctx = a.prompt + a.decode // 2
     bpt = decode_bytes_per_token(spec, ctx, world)
     ms_tok = dec_ms / (a.steps * n_dec)
+    persistent = eng.decode_persistent()
+    seg_roof = None
+    if persistent and world == 1 and not a.no_roofline:
+        seg_roof = segment_roofline(eng, spec, *peaks())
     step_roof = {"bytes_per_token_per_gpu": bpt, "ms_per_token": ms_tok,
                  "achieved_gbs": bpt / (ms_tok * 1e-3) / 1e9, "peak_gbs": hbm,
                  "frac": bpt / (ms_tok * 1e-3) / 1e9 / hbm, "frac_of_8000": bpt / (ms_tok * 1e-3) / 1e9 / 8000.0,
@@ -365,9 +383,17 @@ def bench_ours(a):
         if pg:
             pg.barrier()
         return
-    roof = gemv_roofline(spec, hbm, peak_kind) if world == 1 and not a.no_roofline else None
-    per_layer_kernels = 5 if world == 1 else 5
-    launches_per_token = spec.layers * per_layer_kernels + 2
+    roof = seg_roof
+    if roof is None and world == 1 and not a.no_roofline:
+        roof = gemv_roofline(spec, hbm, peak_kind)
+    # decode launches per token: persistent path = one GEMV segment per layer
+    # plus one, attention per layer, sampler; per-op graph = QKV, attention,
+    # O, gate-up, down per layer (+ residual adds with tensor parallelism),
+    # lm_head, sampler
+    if persistent:
+        launches_per_token = 2 * spec.layers + 2
+    else:
+        launches_per_token = spec.layers * (5 if world == 1 else 7) + 2
     prefill_launches = 1 + spec.layers * 8 + 1
     gpu_launches = a.steps * (prefill_launches + 1 + n_dec * launches_per_token)
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
@@ -376,7 +402,8 @@ def bench_ours(a):
             "data": "synthetic (seeded random-init N(0,0.02) weights, uniform-random prompt ids)",
             "config": {"workload": f"{a.preset}-shaped FP16{f' ({a.layers} layers)' if a.layers else ''}, batch 1, prompt {a.prompt}, {a.decode} generated tokens, "
                                    f"top-k {WORKLOAD['top_k']}, temperature {WORKLOAD['temperature']}",
-                       "parallelism": f"tp{world}", "l2": "weights 6.4 GB >> 126 MB L2 (no flush needed)",
+                       "parallelism": f"tp{world}", "decode_path": "persistent GEMV segments" if persistent else "per-op graph",
+                       "l2": "weights 6.4 GB >> 126 MB L2 (no flush needed)",
                        "timing": "CUDA events on the engine stream; value = decode tokens / decode time"},
             "prefill_tok_s": prefill_tps, "decode_roofline": step_roof, "roofline": roof,
             "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -1346,7 +1346,7 @@ int ylm_options_default(ylm_engine_options *o)
     o->init_std = 0.02;
     o->zero_kv_on_begin = 1;
     o->prefill_tensor_cores = 1;
-    o->decode_persistent = 0;
+    o->decode_persistent = 1;
     return YLM_OK;
 }
 
@@ -1714,6 +1714,51 @@ int ylm_decode_path(ylm_engine *e, int32_t *persistent)
         return YLM_INVALID_ARG;
     *persistent = e->ds_on ? 1 : 0;
     return YLM_OK;
+}
+
+int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per_launch, double *weight_bytes)
+{
+    return guarded([&]() -> int {
+        if (!e || iters <= 0 || !ms_per_launch || !weight_bytes)
+            fail(YLM_INVALID_ARG, "bad argument");
+        if (!e->ds_on)
+            return (int)YLM_UNSUPPORTED;
+        if (layer < 0 || layer >= e->L)
+            fail(YLM_INVALID_ARG, "layer out of range");
+        CK(cudaSetDevice(e->dev));
+        // segment layer + 1 runs layer's O, gate-up, down and the next QKV (or the lm_head)
+        // each timed launch must be its own barrier generation: this copy of
+        // the segment advances *gen at exit (the segment has four phases, so
+        // CTA 0 has passed a wait of the launch by then); afterwards every
+        // counter is reset, which keeps the next decode step consistent
+        DsArgs d = e->ds_seg[layer + 1];
+        d.last = 1;
+        std::vector<DsPhase> ph(d.p1 - d.p0);
+        CK(cudaMemcpy(ph.data(), e->ds_ph + d.p0, sizeof(DsPhase) * ph.size(), cudaMemcpyDeviceToHost));
+        double bytes = 0;
+        for (const DsPhase &p : ph)
+            bytes += 2.0 * p.N * p.K;
+        cudaEvent_t a, b;
+        CK(cudaEventCreate(&a));
+        CK(cudaEventCreate(&b));
+        auto launch_one = [&]() { CK(ds_launch(d, e->ds_smem, e->sms, e->st)); };
+        launch_one(); // warm
+        CK(cudaEventRecord(a, e->st));
+        for (int i = 0; i < iters; i++)
+            launch_one();
+        CK(cudaEventRecord(b, e->st));
+        CK(cudaEventSynchronize(b));
+        float ms = 0;
+        CK(cudaEventElapsedTime(&ms, a, b));
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        CK(cudaMemsetAsync(e->ds_bar, 0, sizeof(unsigned) * e->ds_nph, e->st));
+        CK(cudaMemsetAsync(e->ds_gen, 0, sizeof(unsigned), e->st));
+        e->pull_state_sync();
+        *ms_per_launch = ms / iters;
+        *weight_bytes = bytes;
+        return YLM_OK;
+    });
 }
 
 int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)

@@ -142,6 +142,7 @@ SIGNATURES = {
     "ylm_time_decode": (ctypes.c_int, [_P, ctypes.c_int32, _F64P]),
     "ylm_last_prefill_ms": (ctypes.c_int, [_P, _F64P]),
     "ylm_decode_path": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32)]),
+    "ylm_time_segment": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _F64P, _F64P]),
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
     "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_decode_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
@@ -366,6 +367,12 @@ class Engine:
         st = lib().ylm_time_decode(self._h, iters, ctypes.byref(ms))
         check(st, "ylm_time_decode")
         return ms.value
+
+    def time_segment(self, layer: int, iters: int):
+        """(ms per launch, weight bytes) of one persistent GEMV segment."""
+        ms, nb = ctypes.c_double(), ctypes.c_double()
+        check(lib().ylm_time_segment(self._h, layer, iters, ctypes.byref(ms), ctypes.byref(nb)), "ylm_time_segment")
+        return ms.value, nb.value
 
     def decode_persistent(self) -> bool:
         """True when decode steps run as one cooperative kernel."""
