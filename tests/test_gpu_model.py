@@ -162,6 +162,16 @@ def test_persistent_long_context_and_decode_loop():
     np.testing.assert_array_equal(rp, rg)
     assert ep.time_decode(8) > 0 and eg.time_decode(8) > 0
     np.testing.assert_array_equal(ep.logits(), eg.logits())
+    # timing one segment overwrites the workspace and resets the barrier
+    # counters; the following decode steps must be unaffected
+    ms, nbytes = ep.time_segment(0, 4)
+    assert ms > 0 and nbytes > 0
+    tok = S.greedy(eg.logits())
+    for _ in range(3):
+        ep.infer([tok])
+        eg.infer([tok])
+        np.testing.assert_array_equal(ep.logits(), eg.logits())
+        tok = S.greedy(eg.logits())
     ep.close()
     eg.close()
 

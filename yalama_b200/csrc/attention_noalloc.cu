@@ -26,6 +26,7 @@
 #include "ylm_kernels.h"
 #include "../../include/yalama_b200.h"
 
+#include <cstdio>
 #include <mutex>
 
 namespace ylm {
@@ -108,12 +109,22 @@ extern "C" int ylm_k_decode_attention_noalloc(const void *qkv, const void *q_nor
         prepared[dev] = true;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // an error left by an unrelated earlier runtime call must not be taken
+    // for this call's launch error
+    const cudaError_t stale = cudaGetLastError();
     StepState *state = static_cast<StepState *>(base);
     float *partial = reinterpret_cast<float *>(static_cast<char *>(base) + state_bytes);
     int *tickets = reinterpret_cast<int *>(static_cast<char *>(base) + state_bytes + part_bytes);
     noalloc_reset_kernel<<<1, 1, 0, s>>>(state, tickets, hkv, slot, rope_pos);
-    if (cudaGetLastError() != cudaSuccess)
+    cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess)
+    {
+        char msg[160];
+        snprintf(msg, sizeof(msg), "reset launch: %s (earlier pending error: %s)", cudaGetErrorName(le),
+                 cudaGetErrorName(stale));
+        set_last_error(msg);
         return YLM_CUDA_ERROR;
+    }
     AttnArgs a;
     a.qkv = static_cast<const __half *>(qkv);
     a.q_norm = static_cast<const __half *>(q_norm);
@@ -133,5 +144,15 @@ extern "C" int ylm_k_decode_attention_noalloc(const void *qkv, const void *q_nor
     a.out = static_cast<__half *>(out);
     a.state = state;
     a.err = &state->err;
-    return attn_decode_launch(a, s, false) == cudaSuccess ? YLM_OK : YLM_CUDA_ERROR;
+    le = attn_decode_launch(a, s, false);
+    if (le != cudaSuccess)
+    {
+        char msg[160];
+        snprintf(msg, sizeof(msg), "attention launch: %s (earlier pending error: %s)", cudaGetErrorName(le),
+                 cudaGetErrorName(stale));
+        set_last_error(msg);
+        return YLM_CUDA_ERROR;
+    }
+    set_last_error("");
+    return YLM_OK;
 }

@@ -77,6 +77,12 @@ struct YlmError : std::runtime_error
             fail(YLM_COMM_ERROR, "%s:%d %s: %s", __FILE__, __LINE__, #call, ncclGetErrorString(r_));                  \
     } while (0)
 
+} // namespace
+
+// for the kernel-level entry points outside this file
+void ylm::set_last_error(const char *msg) { g_last_error = msg ? msg : ""; }
+
+namespace {
 template <typename F> int guarded(F &&f)
 {
     try
@@ -344,7 +350,8 @@ struct ylm_engine
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
                         (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_ph,
                         (void *)ds_bar, (void *)ds_gen})
-            if (p)
+            // logits_local is logits itself without tensor parallelism: free once
+            if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
         wblob = nullptr;
         kc = vc = nullptr;

@@ -175,6 +175,9 @@ cudaError_t ds_launch(const DsArgs &a, size_t smem, int grid, cudaStream_t s);
 // Shared-memory opt-in of every kernel on the current device (idempotent).
 cudaError_t kernels_prepare();
 
+// Message returned by ylm_last_error() on the calling thread (kernel-level entry points).
+void set_last_error(const char *msg);
+
 // ------------------------------------------------------------------ prefill (T tokens)
 cudaError_t embed_rows_launch(const int64_t *ids, int T, const __half *emb, int64_t vocab, int H, __half *x, int *err,
                               cudaStream_t s);
