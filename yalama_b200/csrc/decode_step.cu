@@ -6,34 +6,37 @@
 // last segment ends with the lm_head. They replace the per-op chain of
 // src/models/ModelBase.cpp:566-586 (decode branch of ModelBase::Infer) ->
 // ModelBase::Forward (:403-466) -> per-layer attention / FFN (:724-838); the
-// attention between segments is attn_decode_kernel (attention.cu).
+// attention between segments is attn_cluster_kernel (attention.cu).
 //
 // Why persistent: at batch 1 each projection is a GEMV that streams its
 // weights once. Run as separate launches, every kernel starts cold (launch,
 // first-load latency, tail), several microseconds per weight matrix. Here one
-// CTA per SM stays resident for a whole segment; consecutive projections are
-// separated by a grid-wide barrier (one arrival counter per phase), and each
-// warp keeps the next DS_D - 1 tasks' weights in flight in registers,
-// including the first tasks of the next projection while the barrier is
-// pending: weights do not depend on the activations, so their HBM reads never
-// wait for the barrier. (Attention stays a separate kernel: folded into this
-// one, its registers pushed the GEMV loop into spills and slowed every phase.)
+// CTA per SM stays resident for a whole segment, and each warp keeps the next
+// DS_D - 1 tasks' weights in flight in registers, including the first tasks
+// of the next projection while that projection's input is not ready yet:
+// weights do not depend on the activations, so their HBM reads never wait.
+// (Attention stays a separate kernel: folded into this one, its registers
+// pushed the GEMV loop into spills and slowed every phase.)
+//
+// Activations inside a segment carry their own readiness. The residual stream
+// and the SwiGLU activations are 32-bit words, FP16 value in the low half and
+// a tag in the high half naming the step and the phase that wrote it; a
+// prologue polls exactly the words it needs until their tags match (one L2
+// round trip after the producer's store), with no grid barrier between
+// phases. Every phase consumes the whole output of the previous one, so by the
+// time a CTA writes a buffer again, every CTA has finished reading it (each
+// reader wrote an output of a later phase that the writer consumed).
 //
 // The projections reproduce the per-op kernels bit for bit: the GEMV tasks
 // (one row x 2048 columns, FP32 fused multiply-adds in column order, warp
 // butterfly, per-row chunk sums in order), the RMSNorm sum order and the
 // epilogue roundings are the same.
 //
-// Data produced inside the launch (the residual stream, the SwiGLU
-// activations, qkv) is read through L2 only (ld.global.cg), since an SM's L1
-// may still hold the previous layer's values at the same addresses. Weights,
-// norms and the embedding are constant and use the streaming path.
-//
-// The barrier counters are never reset: in decode step n (n = *gen at entry)
-// a phase's barrier is passed once its counter reaches C * (n + 1); CTA 0 of
-// the step's last segment increments *gen at exit. Every wait is bounded
+// Weights, norms and the embedding are constant and use the streaming path;
+// activations are read through L2 only (ld.global.cg). Every wait is bounded
 // (YLM_WAIT_LIMIT_NS) and records YLM_DEV_ERR_TIMEOUT_PEER in the step
-// state's error word; the host then resets the counters.
+// state's error word; after any recorded error the remaining waits give up at
+// once, and the host clears the tagged buffers.
 #include "ylm_common.cuh"
 #include "ylm_kernels.h"
 #include <algorithm>
@@ -92,7 +95,6 @@ extern __shared__ __align__(16) uint8_t ds_smem[];
 struct DsSmem
 {
     DsTab *tab;
-    uint8_t *work;
     __half *xs;
     float *part, *red;
     __half *xr;
@@ -102,74 +104,83 @@ __device__ __forceinline__ DsSmem ds_smem_map(const DsArgs &a)
 {
     DsSmem m;
     m.tab = reinterpret_cast<DsTab *>(ds_smem);
-    m.work = ds_smem + a.tab_bytes;
-    m.xs = reinterpret_cast<__half *>(m.work);
-    m.part = reinterpret_cast<float *>(m.work + (size_t)a.kpad_max * 2);
+    uint8_t *work = ds_smem + a.tab_bytes;
+    m.xs = reinterpret_cast<__half *>(work);
+    m.part = reinterpret_cast<float *>(work + (size_t)a.kpad_max * 2);
     m.red = m.part + a.part_max;
     m.xr = reinterpret_cast<__half *>(ds_smem + a.tab_bytes + a.work_bytes);
     return m;
 }
 
-// ------------------------------------------------------------ grid barrier
-__device__ __forceinline__ void ds_arrive(const DsArgs &a, int i, int tid)
+// ------------------------------------------------------------ tagged activations
+// The tag of phase q in step `gen`: distinct for every phase of a step and
+// between consecutive steps (a word is rewritten at least once per step).
+__device__ __forceinline__ uint32_t ds_tag(unsigned gen, int nph, int q)
 {
-    named_bar_sync(1, DS_THREADS); // every thread's writes of phase i are done
-    if (tid == 0)
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar + i) : "memory");
+    return ((gen * (unsigned)nph + (unsigned)q + 1u) & 0xffffu) << 16;
 }
 
-__device__ __forceinline__ void ds_poll(const DsArgs &a, int i, unsigned target)
+__device__ __forceinline__ uint32_t ds_tagged(uint32_t tag, __half v)
 {
-    uint64_t t0 = 0;
-    for (int n = 0;; n++)
+    return tag | (uint32_t)__half_as_ushort(v);
+}
+
+// 8 tagged words at w (16-byte aligned) -> 8 halves, once every tag is `want`.
+// Bounded: after YLM_WAIT_LIMIT_NS, or at once after any recorded error, the
+// current words are used.
+__device__ __forceinline__ uint4 ds_read_tagged8(const DsArgs &a, const uint32_t *w, uint32_t want)
+{
+    uint4 lo = ds_ldcg16(w), hi = ds_ldcg16(w + 4);
+    auto ready = [&]() {
+        return ((lo.x & 0xffff0000u) == want) & ((lo.y & 0xffff0000u) == want) & ((lo.z & 0xffff0000u) == want) &
+               ((lo.w & 0xffff0000u) == want) & ((hi.x & 0xffff0000u) == want) & ((hi.y & 0xffff0000u) == want) &
+               ((hi.z & 0xffff0000u) == want) & ((hi.w & 0xffff0000u) == want);
+    };
+    if (!ready())
     {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar + i) : "memory");
-        if ((int)(v - target) >= 0)
-            break;
-        if (n == 0)
-            t0 = globaltimer_ns();
-        else if ((n & 63) == 0)
+        const uint64_t t0 = globaltimer_ns();
+        for (int n = 1;; n++)
         {
-            // after any error (an earlier expired wait included) give up at
-            // once, so a failed step ends in one wait limit, not one per phase
-            if (*reinterpret_cast<volatile int *>(a.err) != 0)
+            // back off: every waiting thread of every CTA polls, and those L2
+            // reads compete with the weight stream
+            __nanosleep(256);
+            lo = ds_ldcg16(w);
+            hi = ds_ldcg16(w + 4);
+            if (ready())
                 break;
-            if (globaltimer_ns() - t0 > YLM_WAIT_LIMIT_NS)
+            if ((n & 31) == 0)
             {
-                atomicExch(a.err, YLM_DEV_ERR_TIMEOUT_PEER);
-                break;
+                if (*reinterpret_cast<volatile int *>(a.err) != 0)
+                    break;
+                if (globaltimer_ns() - t0 > YLM_WAIT_LIMIT_NS)
+                {
+                    atomicExch(a.err, YLM_DEV_ERR_TIMEOUT_PEER);
+                    break;
+                }
             }
         }
     }
-}
-
-__device__ __forceinline__ void ds_wait(const DsArgs &a, int i, unsigned target, int tid)
-{
-    if (tid == 0)
-        ds_poll(a, i, target);
-    named_bar_sync(1, DS_THREADS);
+    uint4 o;
+    o.x = (lo.x & 0xffffu) | (lo.y << 16);
+    o.y = (lo.z & 0xffffu) | (lo.w << 16);
+    o.z = (hi.x & 0xffffu) | (hi.y << 16);
+    o.w = (hi.z & 0xffffu) | (hi.w << 16);
+    return o;
 }
 
 // ------------------------------------------------------------ GEMV phases
-// Input vector of phase p into shared memory (all threads). The RMSNorm sum
-// runs on threads 0-255 with the per-op kernel's order. `xr`: this CTA's rows
-// of the residual stream (see ds_epilogue).
-__device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, int kpad, __half *xs, float *red,
-                                            __half *xr, int tid)
+// Input vector of phase p into shared memory (all threads): polled from the
+// tagged words a previous phase of this launch wrote, or loaded from an
+// untagged buffer a previous launch wrote, or gathered from the embedding.
+// The RMSNorm sum runs on threads 0-255 with the per-op kernel's order. `xr`:
+// this CTA's rows of the residual stream (see ds_epilogue).
+__device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, int q, int kpad, unsigned gen,
+                                            __half *xs, float *red, __half *xr, int tid)
 {
     const int K = p.K;
     const int warp = tid >> 5, lane = tid & 31;
-    if (p.pro == PRO_VEC)
-    {
-        for (int i = tid * 8; i < kpad; i += DS_THREADS * 8)
-            *reinterpret_cast<uint4 *>(xs + i) = i < K ? ds_ldcg16(p.x + i) : make_uint4(0, 0, 0, 0);
-        named_bar_sync(1, DS_THREADS);
-        return;
-    }
-    // raw input into shared memory (one global round trip), then the norm in place
-    const __half *src = p.x;
     const bool from_emb = p.pro == PRO_EMBED_RMSNORM;
+    const __half *src = p.x;
     if (from_emb)
     {
         int64_t tok = a.state->token;
@@ -181,28 +192,40 @@ __device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, i
         }
         src = a.emb + tok * (int64_t)K;
     }
+    const uint32_t want = p.xt ? ds_tag(gen, a.nph, p.src) : 0u;
     for (int i = tid * 8; i < kpad; i += DS_THREADS * 8)
     {
         uint4 v = make_uint4(0, 0, 0, 0);
         if (i < K)
-            v = from_emb ? *reinterpret_cast<const uint4 *>(src + i) : ds_ldcg16(src + i);
+        {
+            if (p.xt)
+                v = ds_read_tagged8(a, p.xt + i, want);
+            else if (from_emb)
+                v = *reinterpret_cast<const uint4 *>(src + i);
+            else
+                v = ds_ldcg16(src + i);
+        }
         *reinterpret_cast<uint4 *>(xs + i) = v;
     }
     named_bar_sync(1, DS_THREADS);
     if (from_emb)
     {
         // this CTA's rows of the residual stream start as the embedding row:
-        // the global copy (read by every CTA's RMSNorm) and the CTA's own copy
+        // its own copy, and the tagged words the next segment seeds from
+        const uint32_t tag = ds_tag(gen, a.nph, q);
         const int xr0 = (int)((long long)a.hidden * blockIdx.x / gridDim.x);
         const int xrn = (int)((long long)a.hidden * (blockIdx.x + 1) / gridDim.x) - xr0;
         for (int r = tid; r < xrn; r += DS_THREADS)
         {
             const __half v = xs[xr0 + r];
             xr[r] = v;
-            p.resid[xr0 + r] = v;
+            p.resid_t[xr0 + r] = ds_tagged(tag, v);
         }
     }
-    // sum of squares on threads 0-255 in the per-op kernel's order
+    if (p.pro == PRO_VEC)
+        return;
+    // (the prefetched weights of the coming tasks are live in registers here:
+    // keep this code's own working set small, one half2 at a time)
     if (tid < 256)
     {
         float ss = 0.f;
@@ -250,9 +273,10 @@ __device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, i
     named_bar_sync(1, DS_THREADS);
 }
 
-// Row sums of the chunk partials in order, then the epilogue of the per-op kernel.
+// Row sums of the chunk partials in order, then the epilogue of the per-op
+// kernel; activations consumed inside the launch are written tagged.
 __device__ __forceinline__ void ds_epilogue(const DsPhase &p, const DsTab &t, const float *part, __half *xr,
-                                            int hidden, int tid)
+                                            uint32_t tag, int tid)
 {
     named_bar_sync(1, DS_THREADS); // all partials of the phase are in shared memory
     if (p.epi == EPI_SWIGLU)
@@ -267,7 +291,7 @@ __device__ __forceinline__ void ds_epilogue(const DsPhase &p, const DsTab &t, co
             }
             const float g = rh(gs), u = rh(us);
             const float sg = rh(g / (1.0f + expf(-g)));
-            p.out[(t.r0 + 2 * q) >> 1] = f2h(sg * u);
+            p.out_t[(t.r0 + 2 * q) >> 1] = ds_tagged(tag, f2h(sg * u));
         }
         return;
     }
@@ -283,27 +307,24 @@ __device__ __forceinline__ void ds_epilogue(const DsPhase &p, const DsTab &t, co
                 y = rh(y) + h2f(p.bias[row]);
             p.out[row] = f2h(y);
         }
-        else if (p.N == hidden)
+        else
         {
             // residual stream: every residual phase has N = H and the same row
             // split, so this CTA alone updates these rows and keeps them in
-            // shared memory (its layer-0 prologue seeded them)
+            // shared memory (seeded at launch entry)
             const __half v = f2h(h2f(xr[r]) + rh(y));
             xr[r] = v;
-            p.resid[row] = v;
+            p.resid_t[row] = ds_tagged(tag, v);
         }
-        else
-            p.resid[row] = f2h(h2f(__ldcg(p.resid + row)) + rh(y));
     }
 }
 
 // A run of consecutive GEMV phases [i0, i1). Each warp walks its task stream
-// (phase, task = warp, warp + 16, ...) with a ring of DS_D register buffers
+// (phase, task = warp, warp + 12, ...) with a ring of DS_D register buffers
 // whose roles are fixed by unrolling, so a buffer is never copied while its
-// loads are in flight. `pending`: the barrier of phase i0 - 1 has been arrived
-// at but not waited for; the first loads are issued before that wait. The
-// barrier of the last phase is left pending for the caller.
-__device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, bool pending, unsigned target, int tid)
+// loads are in flight; the first tasks of a phase are loaded while the
+// previous phase is still finishing.
+__device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsigned gen, int tid)
 {
     const DsSmem sm = ds_smem_map(a);
     const DsTab *tab = sm.tab;
@@ -340,19 +361,25 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, bool
 #pragma unroll
     for (int d = 0; d < DS_D - 1; d++)
         load(buf[d]);
-    if (pending)
-        ds_wait(a, i0 - 1, target, tid);
+    // this CTA's rows of the residual stream, as the previous launch left them
+    // (at most one per thread): loaded now, stored after the first prologue so
+    // the two L2 round trips overlap (a layer-0 embedding prologue replaces them)
+    const int xr0 = (int)((long long)a.hidden * blockIdx.x / gridDim.x);
+    const int xrn = (int)((long long)a.hidden * (blockIdx.x + 1) / gridDim.x) - xr0;
+    uint32_t xrv = tid < xrn ? __ldcg(a.xt + xr0 + tid) : 0u;
     int cur = i0;
-    ds_prologue(a, a.ph[cur], tab[cur].nkc * DS_KC, xs, red, xr, tid);
+    if (a.ph[cur].pro == PRO_EMBED_RMSNORM)
+        xrv = 0u; // (not needed: the prologue writes the rows)
+    ds_prologue(a, a.ph[cur], cur, tab[cur].nkc * DS_KC, gen, xs, red, xr, tid);
+    if (tid < xrn && a.ph[i0].pro != PRO_EMBED_RMSNORM)
+        xr[tid] = __ushort_as_half((unsigned short)(xrv & 0xffffu));
+    // (the first epilogue starts with a barrier, which publishes xr)
     // finish phase `cur` (every warp is past its tasks) and open the next one
     auto advance = [&]() {
-        ds_epilogue(a.ph[cur], tab[cur], part, xr, a.hidden, tid);
-        ds_arrive(a, cur, tid);
-        if (cur + 1 < i1)
-            ds_wait(a, cur, target, tid);
+        ds_epilogue(a.ph[cur], tab[cur], part, xr, ds_tag(gen, a.nph, cur), tid);
         cur++;
         if (cur < i1)
-            ds_prologue(a, a.ph[cur], tab[cur].nkc * DS_KC, xs, red, xr, tid);
+            ds_prologue(a, a.ph[cur], cur, tab[cur].nkc * DS_KC, gen, xs, red, xr, tid);
     };
     for (;;)
     {
@@ -390,15 +417,12 @@ done:
 }
 
 // ------------------------------------------------------------ the kernel
-// Phases [a.p0, a.p1) of the table, all GEMV. Phase-table rows outside the
-// range are not touched; the per-CTA table covers the whole step (cheap).
+// Phases [a.p0, a.p1) of the step's table, all GEMV.
 __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsArgs a)
 {
     DsTab *tab = reinterpret_cast<DsTab *>(ds_smem);
-    const DsSmem sm = ds_smem_map(a);
     const int tid = threadIdx.x, C = gridDim.x, c = blockIdx.x;
     const unsigned gen = *reinterpret_cast<volatile const unsigned *>(a.gen);
-    const unsigned target = (unsigned)C * (gen + 1u);
 
     for (int i = a.p0 + tid; i < a.p1; i += DS_THREADS)
     {
@@ -420,19 +444,11 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
         t.ntask = t.rows * t.nkc;
         tab[i] = t;
     }
-    // this CTA's rows of the residual stream, as the previous launch left
-    // them (a layer-0 embedding prologue replaces them)
-    {
-        const int xr0 = (int)((long long)a.hidden * c / C);
-        const int xrn = (int)((long long)a.hidden * (c + 1) / C) - xr0;
-        for (int r = tid; r < xrn; r += DS_THREADS)
-            sm.xr[r] = __ldcg(a.x + xr0 + r);
-    }
     __syncthreads();
 
-    ds_segment(a, a.p0, a.p1, false, target, tid);
-    // in the step's last segment every CTA has arrived at an earlier phase of
-    // this launch, so all have read *gen
+    ds_segment(a, a.p0, a.p1, gen, tid);
+    // the step's last segment ends with a phase whose input is every CTA's
+    // output of an earlier phase of this launch, so all CTAs have read *gen
     if (a.last && c == 0 && tid == 0)
         *a.gen = gen + 1u;
 }

@@ -306,7 +306,8 @@ struct ylm_engine
     size_t ds_smem = 0;
     int ds_nph = 0;
     DsPhase *ds_ph = nullptr;
-    unsigned *ds_bar = nullptr, *ds_gen = nullptr;
+    uint32_t *ds_xt = nullptr, *ds_actt = nullptr; // tagged residual stream and SwiGLU activations
+    unsigned *ds_gen = nullptr;
     std::vector<DsArgs> ds_seg;
 
     bool ready = false;
@@ -349,7 +350,7 @@ struct ylm_engine
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
                         (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_ph,
-                        (void *)ds_bar, (void *)ds_gen})
+                        (void *)ds_xt, (void *)ds_actt, (void *)ds_gen})
             // logits_local is logits itself without tensor parallelism: free once
             if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
@@ -731,9 +732,12 @@ struct ylm_engine
         CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
         if (!coop)
             return;
+        ds_xt = dalloc<uint32_t>(H);
+        ds_actt = dalloc<uint32_t>(inter);
         std::vector<DsPhase> ph;
-        auto gemv = [&](int pro, int epi, const __half *w, int N, int K, const __half *in, const __half *nw,
-                        __half *out, const __half *bias, __half *resid) {
+        // in: plain input from an earlier launch; it/src: tagged input written by phase src
+        auto gemv = [&](int pro, int epi, const __half *w, int N, int K, const __half *in, const uint32_t *it,
+                        int src, const __half *nw, __half *out, uint32_t *out_t, const __half *bias) {
             DsPhase p{};
             p.pro = pro;
             p.epi = epi;
@@ -741,27 +745,39 @@ struct ylm_engine
             p.N = N;
             p.K = K;
             p.x = in;
+            p.xt = it;
+            p.src = src;
             p.norm_w = nw;
             p.out = out;
+            p.out_t = out_t;
             p.bias = bias;
-            p.resid = resid;
+            p.resid_t = ds_xt;
             ph.push_back(p);
+            return (int)ph.size() - 1;
         };
         // phase order: QKV0 | O0 GU0 D0 QKV1 | ... | O(L-1) GU D lm_head
         std::vector<int> cut; // segment boundaries
         cut.push_back(0);
+        int down = -1; // the phase that last wrote the residual stream
         for (int l = 0; l < L; l++)
         {
             Layer &y = layers[l];
-            gemv(l == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM, EPI_STORE, y.wqkv, qkv_rows, H, x, y.ln1, qkv, y.bqkv, x);
+            if (l == 0)
+                gemv(PRO_EMBED_RMSNORM, EPI_STORE, y.wqkv, qkv_rows, H, nullptr, nullptr, 0, y.ln1, qkv, nullptr,
+                     y.bqkv);
+            else
+                gemv(PRO_RMSNORM, EPI_STORE, y.wqkv, qkv_rows, H, nullptr, ds_xt, down, y.ln1, qkv, nullptr, y.bqkv);
             cut.push_back((int)ph.size()); // attention of layer l runs here
-            gemv(PRO_VEC, EPI_RESID, y.wo, H, hq * D, att, nullptr, nullptr, nullptr, x);
-            gemv(PRO_RMSNORM, EPI_SWIGLU, y.wgu, 2 * inter, H, x, y.ln2, act, nullptr, nullptr);
-            gemv(PRO_VEC, EPI_RESID, y.wd, H, inter, act, nullptr, nullptr, nullptr, x);
+            const int o = gemv(PRO_VEC, EPI_RESID, y.wo, H, hq * D, att, nullptr, 0, nullptr, nullptr, nullptr, nullptr);
+            const int gu = gemv(PRO_RMSNORM, EPI_SWIGLU, y.wgu, 2 * inter, H, nullptr, ds_xt, o, y.ln2, nullptr, ds_actt,
+                                nullptr);
+            down = gemv(PRO_VEC, EPI_RESID, y.wd, H, inter, nullptr, ds_actt, gu, nullptr, nullptr, nullptr, nullptr);
         }
-        gemv(PRO_RMSNORM, EPI_STORE, lm, (int)v_local, H, x, fnorm, logits_local, nullptr, nullptr);
+        gemv(PRO_RMSNORM, EPI_STORE, lm, (int)v_local, H, nullptr, ds_xt, down, fnorm, logits_local, nullptr, nullptr);
         cut.push_back((int)ph.size());
         const int C = sms;
+        if ((H + C - 1) / C > ds_threads())
+            return; // each thread seeds at most one residual row
         const int kc_cols = ds_task_cols();
         int kpad_max = 0, part_max = 0;
         for (const DsPhase &p : ph)
@@ -786,17 +802,16 @@ struct ylm_engine
         }
         ds_ph = dalloc<DsPhase>(nph);
         CK(cudaMemcpy(ds_ph, ph.data(), sizeof(DsPhase) * nph, cudaMemcpyHostToDevice));
-        ds_bar = dalloc<unsigned>(nph);
         ds_gen = dalloc<unsigned>(1);
         DsArgs d{};
         d.ph = ds_ph;
+        d.nph = nph;
         d.eps = cfg.rms_eps;
         d.emb = emb;
         d.vocab = V;
         d.state = dstate;
-        d.x = x;
+        d.xt = ds_xt;
         d.hidden = H;
-        d.bar = ds_bar;
         d.gen = ds_gen;
         d.err = &dstate->err;
         d.tab_bytes = (int)tab_bytes;
@@ -814,6 +829,15 @@ struct ylm_engine
         ds_nph = nph;
         ds_smem = smem;
         ds_on = true;
+    }
+
+    // Clear the persistent path's step generation and tagged activations, so no
+    // word left by a failed or timing launch can match a coming tag.
+    void ds_reset()
+    {
+        cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
+        cudaMemsetAsync(ds_xt, 0, sizeof(uint32_t) * H, st);
+        cudaMemsetAsync(ds_actt, 0, sizeof(uint32_t) * inter, st);
     }
 
     // ModelBase::CalculateMaxSequenceLength (ModelBase.cpp:312-338)
@@ -1078,11 +1102,8 @@ struct ylm_engine
             // counters may be left mid-step: reset them so the next step starts clean
             cudaMemsetAsync(counters, 0, sizeof(int) * hkv, st);
             cudaMemsetAsync(smp_counter, 0, sizeof(int), st);
-            if (ds_bar)
-            {
-                cudaMemsetAsync(ds_bar, 0, sizeof(unsigned) * ds_nph, st);
-                cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
-            }
+            if (ds_gen)
+                ds_reset();
             cudaStreamSynchronize(st);
             if (e == YLM_DEV_ERR_BAD_TOKEN)
                 fail(YLM_INVALID_ARG, "token id out of range");
@@ -1734,10 +1755,10 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
             fail(YLM_INVALID_ARG, "layer out of range");
         CK(cudaSetDevice(e->dev));
         // segment layer + 1 runs layer's O, gate-up, down and the next QKV (or the lm_head)
-        // each timed launch must be its own barrier generation: this copy of
-        // the segment advances *gen at exit (the segment has four phases, so
-        // CTA 0 has passed a wait of the launch by then); afterwards every
-        // counter is reset, which keeps the next decode step consistent
+        // each timed launch must tag its activations apart from the previous
+        // one's: this copy of the segment advances *gen at exit; afterwards the
+        // generation and the tagged buffers are cleared, which keeps the next
+        // decode step consistent
         DsArgs d = e->ds_seg[layer + 1];
         d.last = 1;
         std::vector<DsPhase> ph(d.p1 - d.p0);
@@ -1759,8 +1780,7 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
         CK(cudaEventElapsedTime(&ms, a, b));
         cudaEventDestroy(a);
         cudaEventDestroy(b);
-        CK(cudaMemsetAsync(e->ds_bar, 0, sizeof(unsigned) * e->ds_nph, e->st));
-        CK(cudaMemsetAsync(e->ds_gen, 0, sizeof(unsigned), e->st));
+        e->ds_reset();
         e->pull_state_sync();
         *ms_per_launch = ms / iters;
         *weight_bytes = bytes;

@@ -140,26 +140,30 @@ struct DsPhase
     int epi;         // GemvEpi
     const __half *w; // [N, K] row-major
     int N, K;
-    const __half *x;      // PRO_VEC input, or the residual stream for the RMSNorm prologues
+    const __half *x;    // PRO_VEC / RMSNorm input written by an earlier launch (plain FP16), or null
+    const uint32_t *xt; // input written tagged by phase `src` of the same launch, or null
+    int src;
     const __half *norm_w; // RMSNorm weight [K]
-    __half *out;          // EPI_STORE / EPI_SWIGLU output
+    __half *out;          // EPI_STORE output (read by a later launch)
+    uint32_t *out_t;      // EPI_SWIGLU output, tagged
     const __half *bias;   // EPI_STORE bias or null
-    __half *resid;        // EPI_RESID target; PRO_EMBED_RMSNORM: each CTA writes its residual rows of
-                          // the embedding row here
+    uint32_t *resid_t;    // EPI_RESID target, the tagged residual stream; PRO_EMBED_RMSNORM: each
+                          // CTA writes its rows of the embedding row here
 };
 struct DsArgs
 {
     const DsPhase *ph; // the step's GEMV phases, device memory
+    int nph;           // phases in the step (tags)
     int p0, p1;        // this launch runs phases [p0, p1)
     int last;          // 1: the step's last segment (advances *gen)
     float eps;
     const __half *emb;
     int64_t vocab;
     const StepState *state;
-    const __half *x;   // residual stream [hidden]
-    int hidden;        // each CTA keeps its rows of it (split like an N = hidden projection)
-    unsigned *bar;     // [phases] arrival counters, monotonic across steps
-    unsigned *gen;     // decode steps completed
+    const uint32_t *xt; // tagged residual stream [hidden]
+    int hidden;         // each CTA keeps its rows of it (split like an N = hidden projection);
+                        // a CTA's rows must not exceed the block size
+    unsigned *gen;      // decode steps completed
     int *err;
     int tab_bytes;  // shared-memory layout: phase table, work area, residual rows
     int work_bytes; // GEMV input vector, partials, RMSNorm scratch
