@@ -88,8 +88,8 @@ __device__ __forceinline__ float ds_dot8(uint4 w, uint4 x, float acc)
 }
 
 // ------------------------------------------------------------ shared memory
-// [phase table | work area (GEMV input, partials, RMSNorm scratch) | this
-// CTA's residual rows].
+// [this CTA's table of the launch's phases | work area (GEMV input, partials,
+// RMSNorm scratch) | this CTA's residual rows].
 extern __shared__ __align__(16) uint8_t ds_smem[];
 
 struct DsSmem
@@ -333,7 +333,7 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
     __half *xr = sm.xr;
     const int warp = tid >> 5, lane = tid & 31;
     int pp = i0, pt = warp; // prefetch cursor
-    while (pp < i1 && pt >= tab[pp].ntask)
+    while (pp < i1 && pt >= tab[pp - a.p0].ntask)
     {
         pp++;
         pt = warp;
@@ -343,8 +343,8 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
     auto load = [&](uint4 *w) {
         if (pp >= i1)
             return;
-        const DsTab &t = tab[pp];
-        const DsPhase &p = a.ph[pp];
+        const DsTab &t = tab[pp - a.p0];
+        const DsPhase &p = a.ph[pp - a.p0];
         const int row = t.r0 + pt / t.nkc, kc = pt % t.nkc;
         const __half *base = p.w + (size_t)row * p.K + kc * DS_KC + lane * 8;
         const int lim = p.K - kc * DS_KC - lane * 8;
@@ -352,7 +352,7 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
         for (int u = 0; u < DS_U; u++)
             w[u] = u * 256 < lim ? ds_ldg_stream(base + u * 256) : make_uint4(0, 0, 0, 0);
         pt += DS_WARPS;
-        while (pp < i1 && pt >= tab[pp].ntask)
+        while (pp < i1 && pt >= tab[pp - a.p0].ntask)
         {
             pp++;
             pt = warp;
@@ -368,18 +368,18 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
     const int xrn = (int)((long long)a.hidden * (blockIdx.x + 1) / gridDim.x) - xr0;
     uint32_t xrv = tid < xrn ? __ldcg(a.xt + xr0 + tid) : 0u;
     int cur = i0;
-    if (a.ph[cur].pro == PRO_EMBED_RMSNORM)
+    if (a.ph[cur - a.p0].pro == PRO_EMBED_RMSNORM)
         xrv = 0u; // (not needed: the prologue writes the rows)
-    ds_prologue(a, a.ph[cur], cur, tab[cur].nkc * DS_KC, gen, xs, red, xr, tid);
-    if (tid < xrn && a.ph[i0].pro != PRO_EMBED_RMSNORM)
+    ds_prologue(a, a.ph[cur - a.p0], cur, tab[cur - a.p0].nkc * DS_KC, gen, xs, red, xr, tid);
+    if (tid < xrn && a.ph[i0 - a.p0].pro != PRO_EMBED_RMSNORM)
         xr[tid] = __ushort_as_half((unsigned short)(xrv & 0xffffu));
     // (the first epilogue starts with a barrier, which publishes xr)
     // finish phase `cur` (every warp is past its tasks) and open the next one
     auto advance = [&]() {
-        ds_epilogue(a.ph[cur], tab[cur], part, xr, ds_tag(gen, a.nph, cur), tid);
+        ds_epilogue(a.ph[cur - a.p0], tab[cur - a.p0], part, xr, ds_tag(gen, a.nph, cur), tid);
         cur++;
         if (cur < i1)
-            ds_prologue(a, a.ph[cur], cur, tab[cur].nkc * DS_KC, gen, xs, red, xr, tid);
+            ds_prologue(a, a.ph[cur - a.p0], cur, tab[cur - a.p0].nkc * DS_KC, gen, xs, red, xr, tid);
     };
     for (;;)
     {
@@ -392,7 +392,7 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
                 goto done;
             load(buf[(d + DS_D - 1) % DS_D]);
             {
-                const DsTab &t = tab[cp];
+                const DsTab &t = tab[cp - a.p0];
                 const int kc = ct % t.nkc;
                 const __half *xk = xs + kc * DS_KC + lane * 8;
                 float acc = 0.f;
@@ -403,7 +403,7 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
                 if (lane == 0)
                     part[ct] = acc; // slot (row ct / nkc, chunk ct % nkc)
                 ct += DS_WARPS;
-                while (cp < i1 && ct >= tab[cp].ntask)
+                while (cp < i1 && ct >= tab[cp - a.p0].ntask)
                 {
                     cp++;
                     ct = warp;
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
 
     for (int i = a.p0 + tid; i < a.p1; i += DS_THREADS)
     {
-        const DsPhase &p = a.ph[i];
+        const DsPhase &p = a.ph[i - a.p0];
         DsTab t;
         if (p.epi == EPI_SWIGLU)
         {
@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
         }
         t.nkc = (p.K + DS_KC - 1) / DS_KC;
         t.ntask = t.rows * t.nkc;
-        tab[i] = t;
+        tab[i - a.p0] = t;
     }
     __syncthreads();
 

@@ -305,7 +305,7 @@ struct ylm_engine
     bool ds_graph_ok = true; // cleared if the cooperative launches cannot be captured
     size_t ds_smem = 0;
     int ds_nph = 0;
-    DsPhase *ds_ph = nullptr;
+    std::vector<DsPhase> ds_phases; // the step's GEMV phases (host copy)
     uint32_t *ds_xt = nullptr, *ds_actt = nullptr; // tagged residual stream and SwiGLU activations
     unsigned *ds_gen = nullptr;
     std::vector<DsArgs> ds_seg;
@@ -349,8 +349,7 @@ struct ylm_engine
                         (void *)qkv, (void *)att, (void *)act, (void *)logits, (void *)logits_local, (void *)ar,
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
-                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_ph,
-                        (void *)ds_xt, (void *)ds_actt, (void *)ds_gen})
+                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen})
             // logits_local is logits itself without tensor parallelism: free once
             if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
@@ -788,7 +787,10 @@ struct ylm_engine
             part_max = std::max(part_max, rows * nkc);
         }
         const int nph = (int)ph.size();
-        const size_t tab_bytes = ((size_t)nph * 16 + 15) & ~(size_t)15;
+        for (size_t k = 0; k + 1 < cut.size(); k++)
+            if (cut[k + 1] - cut[k] > DS_MAX_SEG_PHASES)
+                return;
+        const size_t tab_bytes = (size_t)DS_MAX_SEG_PHASES * 16;
         const size_t work_bytes = ((size_t)kpad_max * 2 + (size_t)part_max * 4 + 32 * 4 + 15) & ~(size_t)15;
         const size_t xr_bytes = ((size_t)(H + C - 1) / C * 2 + 15) & ~(size_t)15;
         const size_t smem = tab_bytes + work_bytes + xr_bytes;
@@ -800,11 +802,8 @@ struct ylm_engine
             cudaGetLastError();
             return;
         }
-        ds_ph = dalloc<DsPhase>(nph);
-        CK(cudaMemcpy(ds_ph, ph.data(), sizeof(DsPhase) * nph, cudaMemcpyHostToDevice));
         ds_gen = dalloc<unsigned>(1);
         DsArgs d{};
-        d.ph = ds_ph;
         d.nph = nph;
         d.eps = cfg.rms_eps;
         d.emb = emb;
@@ -819,11 +818,14 @@ struct ylm_engine
         d.kpad_max = kpad_max;
         d.part_max = part_max;
         ds_seg.clear();
+        ds_phases = ph;
         for (size_t k = 0; k + 1 < cut.size(); k++)
         {
             d.p0 = cut[k];
             d.p1 = cut[k + 1];
             d.last = k + 2 == cut.size() ? 1 : 0;
+            for (int i = d.p0; i < d.p1; i++)
+                d.ph[i - d.p0] = ph[i];
             ds_seg.push_back(d);
         }
         ds_nph = nph;
@@ -1761,11 +1763,9 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
         // decode step consistent
         DsArgs d = e->ds_seg[layer + 1];
         d.last = 1;
-        std::vector<DsPhase> ph(d.p1 - d.p0);
-        CK(cudaMemcpy(ph.data(), e->ds_ph + d.p0, sizeof(DsPhase) * ph.size(), cudaMemcpyDeviceToHost));
         double bytes = 0;
-        for (const DsPhase &p : ph)
-            bytes += 2.0 * p.N * p.K;
+        for (int i = d.p0; i < d.p1; i++)
+            bytes += 2.0 * e->ds_phases[i].N * e->ds_phases[i].K;
         cudaEvent_t a, b;
         CK(cudaEventCreate(&a));
         CK(cudaEventCreate(&b));

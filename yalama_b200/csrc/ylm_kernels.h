@@ -150,11 +150,12 @@ struct DsPhase
     uint32_t *resid_t;    // EPI_RESID target, the tagged residual stream; PRO_EMBED_RMSNORM: each
                           // CTA writes its rows of the embedding row here
 };
+#define DS_MAX_SEG_PHASES 4
 struct DsArgs
 {
-    const DsPhase *ph; // the step's GEMV phases, device memory
-    int nph;           // phases in the step (tags)
-    int p0, p1;        // this launch runs phases [p0, p1)
+    DsPhase ph[DS_MAX_SEG_PHASES]; // this launch's phases (kernel parameters: constant bank)
+    int nph;                       // phases in the step (tags)
+    int p0, p1;                    // this launch runs the step's phases [p0, p1); ph[i - p0] is phase i
     int last;          // 1: the step's last segment (advances *gen)
     float eps;
     const __half *emb;
