@@ -128,6 +128,8 @@ def args_():
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for profiler captures; not a bench number)")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--decode-path", default="persistent", choices=["persistent", "per-op"],
+                    help="persistent GEMV segments (default) or the per-op graph")
     return ap.parse_args()
 
 
@@ -285,6 +287,7 @@ def bench_ours(a):
     import numpy as np
     import torch
     from yalama_b200 import engine as E
+    from yalama_b200 import tp as TP
     from yalama_b200 import synth
 
     rank, world, local = dist_env()
@@ -298,16 +301,14 @@ def bench_ours(a):
         import datetime
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         pg = dist
-        obj = [E.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nccl_id = obj[0]
+        nccl_id = TP.share_nccl_id(pg, rank)
     spec = synth.PRESETS[a.preset]
     if a.layers:
         import dataclasses
         spec = dataclasses.replace(spec, layers=a.layers)
     cfg = E.config_from_spec(spec)
     eng = E.Engine(None, cfg, nccl_id=nccl_id, device=local, tp_rank=rank, tp_size=world,
-                   init_seed=WORKLOAD["weight_seed"])
+                   init_seed=WORKLOAD["weight_seed"], decode_persistent=int(a.decode_path == "persistent"))
     eng.set_sampling(greedy=False, top_k=WORKLOAD["top_k"], temperature=WORKLOAD["temperature"],
                      seed=WORKLOAD["sample_seed"])
     prompt = synth.prompt_ids(WORKLOAD["prompt_seed"], a.prompt, spec.vocab)
@@ -389,7 +390,7 @@ def bench_ours(a):
     # decode launches per token: persistent path = one GEMV segment per layer
     # plus one, attention per layer, sampler; per-op graph = QKV, attention,
     # O, gate-up, down per layer (+ residual adds with tensor parallelism),
-    # lm_head, sampler
+    # lm_head, sampler; NCCL's all-reduce / all-gather kernels are not counted
     if persistent:
         launches_per_token = 2 * spec.layers + 2
     else:

@@ -91,8 +91,9 @@ typedef struct ylm_engine_options {
     int32_t zero_kv_on_begin; /* 1 (default): BeginInfer zeroes the cache like ModelBase.cpp:302-309 */
     int32_t prefill_tensor_cores; /* 1 (default): tcgen05 GEMMs for prefill; 0: CUDA-core GEMMs */
     int32_t decode_persistent;    /* 1 (default): the projections between two attention launches of a
-                                     decode step run as one cooperative kernel (single GPU; with
-                                     tensor parallelism the per-op graph is used); 0: the per-op graph */
+                                     decode step run as one cooperative kernel; with tensor parallelism
+                                     its O and down epilogues all-reduce over NVLink peer memory;
+                                     0: the per-op graph */
 } ylm_engine_options;
 
 /* ChatSession::Sample parameters (src/ChatSession.cpp:560-593). */
@@ -167,15 +168,15 @@ int ylm_last_prefill_ms(ylm_engine *e, double *ms);
  * (CUDA events on the engine stream; state advanced on the device). */
 int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step);
 /* Which decode path the engine runs: *persistent = 1 when each decode step's
- * forward is one cooperative kernel, 0 for the per-op graph. No counterpart in
+ * projections run as persistent GEMV segments, 0 for the per-op graph. No counterpart in
  * the reference (engine introspection for tests and benchmarks). */
 int ylm_decode_path(ylm_engine *e, int32_t *persistent);
 /* Time `iters` back-to-back launches of one persistent GEMV segment (the
  * projections of layer `layer`: O, gate-up, down and the next layer's QKV, or
  * the lm_head for the last) with CUDA events on the engine stream; writes the
  * segment's weight bytes. Overwrites the decode workspace (call between
- * requests). YLM_UNSUPPORTED on the per-op path. No counterpart in the
- * reference (benchmark support). */
+ * requests). YLM_UNSUPPORTED on the per-op path and with tensor parallelism.
+ * No counterpart in the reference (benchmark support). */
 int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per_launch, double *weight_bytes);
 
 /* ---- kernel-level entry points (device pointers; stream = cudaStream_t or NULL) */

@@ -1,0 +1,102 @@
+"""Tensor parallelism on two GPUs: two processes, one engine each (rank r
+holds 1/2 of every projection), through the C ABI.
+
+With two ranks the all-reduce of FP16 partials is one correctly rounded FP16
+addition per element whichever side computes it, so the persistent path (the
+all-reduce inside the GEMV segments, over NVLink peer memory) and the per-op
+graph (NCCL all-reduce, then a residual add) agree bit for bit. Both stay
+within the logit tolerance of the oracle's single-device FP16 forward."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from oracle.model import OracleModel
+from oracle import sampler as S
+from yalama_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 2e-2
+FAMILIES = {
+    "llama": dict(model_type="llama", tied=False, rope_theta=5e5, heads=8, kv_heads=2),
+    "qwen3": dict(model_type="qwen3"),
+    "qwen2": dict(model_type="qwen2", tied=False),
+}
+PROMPT_LEN, STEPS = 40, 12
+
+
+def gpus():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    import datetime
+    import torch.distributed as dist
+    from yalama_b200 import engine as E
+    from yalama_b200 import tp as TP
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        for fam, kw in FAMILIES.items():
+            spec = synth.tiny_spec(**kw)
+            cfg = E.config_from_spec(spec)
+            prompt = synth.prompt_ids(5, PROMPT_LEN, spec.vocab)
+            for persistent in (0, 1):
+                eng = TP.tp_engine(dist, rank, world, cfg, init_seed=0, decode_persistent=persistent)
+                assert eng.decode_persistent() == bool(persistent)
+                eng.begin_infer()
+                st, _ = eng.infer(prompt)
+                assert st == E.Status.OK
+                rows, toks = [eng.logits()], []
+                for _ in range(STEPS):
+                    tok = S.greedy(rows[-1])
+                    toks.append(tok)
+                    st, _ = eng.infer([tok])
+                    assert st == E.Status.OK
+                    rows.append(eng.logits())
+                # the advance-mode decode loop (graph replays), then one more step
+                assert eng.time_decode(6) > 0
+                loop = eng.logits()
+                if rank == 0:
+                    np.savez(os.path.join(out_dir, f"{fam}_{persistent}.npz"), rows=np.stack(rows),
+                             toks=np.array(toks), loop=loop)
+                eng.close()
+                dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(gpus() < 2, reason="needs 2 GPUs")
+def test_tp2_persistent_and_per_op_agree_and_match_oracle(tmp_path):
+    import torch.multiprocessing as mp
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_rank_main, args=(2, free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for fam, kw in FAMILIES.items():
+        p = np.load(tmp_path / f"{fam}_1.npz")
+        g = np.load(tmp_path / f"{fam}_0.npz")
+        np.testing.assert_array_equal(p["rows"], g["rows"])
+        np.testing.assert_array_equal(p["toks"], g["toks"])
+        np.testing.assert_array_equal(p["loop"], g["loop"])
+        spec = synth.tiny_spec(**kw)
+        orc = OracleModel(spec, synth.model_weights(spec, 0), mode="f16", kv_gb=2)
+        orc.begin_infer()
+        ids = list(synth.prompt_ids(5, PROMPT_LEN, spec.vocab))
+        worst = 0.0
+        for i, row in enumerate(p["rows"]):
+            _, lo = orc.infer(ids)
+            worst = max(worst, float(np.max(np.abs(row - lo))))
+            if i < len(p["toks"]):
+                ids = [int(p["toks"][i])]
+        print(f"{fam} tp2: max |logit diff| vs oracle = {worst:.3e}")
+        assert worst < LOGIT_TOL

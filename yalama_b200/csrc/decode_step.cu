@@ -37,6 +37,14 @@
 // (YLM_WAIT_LIMIT_NS) and records YLM_DEV_ERR_TIMEOUT_PEER in the step
 // state's error word; after any recorded error the remaining waits give up at
 // once, and the host clears the tagged buffers.
+//
+// With tensor parallelism the O and down projections end in an all-reduce
+// fused into their epilogue: each CTA stores its partial rows, tagged, into
+// every rank's mailbox over NVLink (plain peer stores), then sums its rows of
+// all ranks' partials from its own mailbox and adds the residual. O and down
+// use separate mailbox sets: a rank can only reach the next layer's O after
+// receiving every peer's down partials, which each peer sends after reading
+// its O mailbox, so no slot is overwritten before it is read.
 #include "ylm_common.cuh"
 #include "ylm_kernels.h"
 #include <algorithm>
@@ -168,6 +176,34 @@ __device__ __forceinline__ uint4 ds_read_tagged8(const DsArgs &a, const uint32_t
     return o;
 }
 
+// One tagged word (a peer's partial in this rank's mailbox) -> its half.
+__device__ __forceinline__ __half ds_read_tagged1(const DsArgs &a, const uint32_t *w, uint32_t want)
+{
+    uint32_t v = __ldcg(w);
+    if ((v & 0xffff0000u) != want)
+    {
+        const uint64_t t0 = globaltimer_ns();
+        for (int n = 1;; n++)
+        {
+            __nanosleep(256);
+            v = __ldcg(w);
+            if ((v & 0xffff0000u) == want)
+                break;
+            if ((n & 31) == 0)
+            {
+                if (*reinterpret_cast<volatile int *>(a.err) != 0)
+                    break;
+                if (globaltimer_ns() - t0 > YLM_WAIT_LIMIT_NS)
+                {
+                    atomicExch(a.err, YLM_DEV_ERR_TIMEOUT_PEER);
+                    break;
+                }
+            }
+        }
+    }
+    return __ushort_as_half((unsigned short)(v & 0xffffu));
+}
+
 // ------------------------------------------------------------ GEMV phases
 // Input vector of phase p into shared memory (all threads): polled from the
 // tagged words a previous phase of this launch wrote, or loaded from an
@@ -275,8 +311,8 @@ __device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, i
 
 // Row sums of the chunk partials in order, then the epilogue of the per-op
 // kernel; activations consumed inside the launch are written tagged.
-__device__ __forceinline__ void ds_epilogue(const DsPhase &p, const DsTab &t, const float *part, __half *xr,
-                                            uint32_t tag, int tid)
+__device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, const DsTab &t, const float *part,
+                                            __half *xr, uint32_t tag, int tid)
 {
     named_bar_sync(1, DS_THREADS); // all partials of the phase are in shared memory
     if (p.epi == EPI_SWIGLU)
@@ -292,6 +328,34 @@ __device__ __forceinline__ void ds_epilogue(const DsPhase &p, const DsTab &t, co
             const float g = rh(gs), u = rh(us);
             const float sg = rh(g / (1.0f + expf(-g)));
             p.out_t[(t.r0 + 2 * q) >> 1] = ds_tagged(tag, f2h(sg * u));
+        }
+        return;
+    }
+    if (p.epi == EPI_RESID && p.mbox)
+    {
+        // tensor parallel: this rank's partial of the rows (FP16, as the per-op
+        // path's all-reduce input) goes to slot `rank` of every rank's mailbox;
+        // then this CTA sums its rows over all ranks' slots of its own mailbox,
+        // in rank order, and adds the residual, identically on every rank
+        uint32_t *const *mb = a.mb[p.mbox - 1];
+        for (int r = tid; r < t.rows; r += DS_THREADS)
+        {
+            float y = 0.f;
+            for (int c = 0; c < t.nkc; c++)
+                y += part[r * t.nkc + c];
+            const uint32_t w = ds_tagged(tag, f2h(y));
+            const size_t off = (size_t)a.rank * a.hidden + t.r0 + r;
+            for (int q = 0; q < a.tp; q++)
+                mb[q][off] = w;
+        }
+        for (int r = tid; r < t.rows; r += DS_THREADS)
+        {
+            float sum = 0.f;
+            for (int q = 0; q < a.tp; q++)
+                sum += h2f(ds_read_tagged1(a, mb[a.rank] + (size_t)q * a.hidden + t.r0 + r, tag));
+            const __half v = f2h(h2f(xr[r]) + rh(sum));
+            xr[r] = v;
+            p.resid_t[t.r0 + r] = ds_tagged(tag, v);
         }
         return;
     }
@@ -376,7 +440,7 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
     // (the first epilogue starts with a barrier, which publishes xr)
     // finish phase `cur` (every warp is past its tasks) and open the next one
     auto advance = [&]() {
-        ds_epilogue(a.ph[cur - a.p0], tab[cur - a.p0], part, xr, ds_tag(gen, a.nph, cur), tid);
+        ds_epilogue(a, a.ph[cur - a.p0], tab[cur - a.p0], part, xr, ds_tag(gen, a.nph, cur), tid);
         cur++;
         if (cur < i1)
             ds_prologue(a, a.ph[cur - a.p0], cur, tab[cur - a.p0].nkc * DS_KC, gen, xs, red, xr, tid);

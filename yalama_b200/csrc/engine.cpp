@@ -306,6 +306,8 @@ struct ylm_engine
     size_t ds_smem = 0;
     int ds_nph = 0;
     std::vector<DsPhase> ds_phases; // the step's GEMV phases (host copy)
+    uint32_t *ds_mb_local[2] = {nullptr, nullptr};  // this rank's two mailbox sets [tp][H]
+    std::vector<void *> ds_mb_peer;                  // peers' mailboxes mapped through CUDA IPC
     uint32_t *ds_xt = nullptr, *ds_actt = nullptr; // tagged residual stream and SwiGLU activations
     unsigned *ds_gen = nullptr;
     std::vector<DsArgs> ds_seg;
@@ -337,6 +339,15 @@ struct ylm_engine
         if (g_fwd_sample)
             cudaGraphExecDestroy(g_fwd_sample);
         g_fwd = g_fwd_sample = nullptr;
+        for (void *pm : ds_mb_peer)
+            cudaIpcCloseMemHandle(pm);
+        ds_mb_peer.clear();
+        for (uint32_t *&m : ds_mb_local)
+        {
+            if (m)
+                cudaFree(m);
+            m = nullptr;
+        }
         if (comm)
             ncclCommDestroy(comm);
         comm = nullptr;
@@ -719,13 +730,13 @@ struct ylm_engine
     }
 
     // Persistent GEMV segments: one cooperative launch (one CTA per SM) per run
-    // of projections between two attention launches. Single GPU only, and only
-    // where the device can keep one CTA per SM resident; otherwise the per-op
-    // graph.
+    // of projections between two attention launches, where the device can keep
+    // one CTA per SM resident; otherwise the per-op graph. With tensor
+    // parallelism the O and down epilogues all-reduce through peer mailboxes.
     void setup_persistent()
     {
         ds_on = false;
-        if (!opt.decode_persistent || tp != 1)
+        if (!opt.decode_persistent || tp > 8)
             return;
         int coop = 0;
         CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
@@ -768,9 +779,11 @@ struct ylm_engine
                 gemv(PRO_RMSNORM, EPI_STORE, y.wqkv, qkv_rows, H, nullptr, ds_xt, down, y.ln1, qkv, nullptr, y.bqkv);
             cut.push_back((int)ph.size()); // attention of layer l runs here
             const int o = gemv(PRO_VEC, EPI_RESID, y.wo, H, hq * D, att, nullptr, 0, nullptr, nullptr, nullptr, nullptr);
+            ph[o].mbox = tp > 1 ? 1 : 0; // all-reduce of the O partials (tensor parallel)
             const int gu = gemv(PRO_RMSNORM, EPI_SWIGLU, y.wgu, 2 * inter, H, nullptr, ds_xt, o, y.ln2, nullptr, ds_actt,
                                 nullptr);
             down = gemv(PRO_VEC, EPI_RESID, y.wd, H, inter, nullptr, ds_actt, gu, nullptr, nullptr, nullptr, nullptr);
+            ph[down].mbox = tp > 1 ? 2 : 0;
         }
         gemv(PRO_RMSNORM, EPI_STORE, lm, (int)v_local, H, nullptr, ds_xt, down, fnorm, logits_local, nullptr, nullptr);
         cut.push_back((int)ph.size());
@@ -805,6 +818,10 @@ struct ylm_engine
         ds_gen = dalloc<unsigned>(1);
         DsArgs d{};
         d.nph = nph;
+        d.tp = tp;
+        d.rank = rank;
+        if (tp > 1)
+            setup_mailboxes(d);
         d.eps = cfg.rms_eps;
         d.emb = emb;
         d.vocab = V;
@@ -833,6 +850,42 @@ struct ylm_engine
         ds_on = true;
     }
 
+    // Tensor parallel all-reduce mailboxes: two sets of [tp][H] tagged words
+    // per rank; every rank maps every peer's through CUDA IPC (handles
+    // exchanged with one NCCL all-gather), and writes its partials into slot
+    // `rank` of each with plain peer stores over NVLink.
+    void setup_mailboxes(DsArgs &d)
+    {
+        cudaIpcMemHandle_t mine[2];
+        for (int s = 0; s < 2; s++)
+        {
+            ds_mb_local[s] = dalloc<uint32_t>((size_t)tp * H);
+            CK(cudaIpcGetMemHandle(&mine[s], ds_mb_local[s]));
+        }
+        char *dsend = dalloc<char>(sizeof(mine));
+        char *drecv = dalloc<char>(sizeof(mine) * tp);
+        CK(cudaMemcpy(dsend, mine, sizeof(mine), cudaMemcpyHostToDevice));
+        NK(ncclAllGather(dsend, drecv, sizeof(mine), ncclChar, comm, st));
+        CK(cudaStreamSynchronize(st));
+        std::vector<cudaIpcMemHandle_t> all(2 * (size_t)tp);
+        CK(cudaMemcpy(all.data(), drecv, sizeof(mine) * tp, cudaMemcpyDeviceToHost));
+        cudaFree(dsend);
+        cudaFree(drecv);
+        for (int s = 0; s < 2; s++)
+            for (int q = 0; q < tp; q++)
+            {
+                if (q == rank)
+                {
+                    d.mb[s][q] = ds_mb_local[s];
+                    continue;
+                }
+                void *pm = nullptr;
+                CK(cudaIpcOpenMemHandle(&pm, all[2 * (size_t)q + s], cudaIpcMemLazyEnablePeerAccess));
+                ds_mb_peer.push_back(pm);
+                d.mb[s][q] = static_cast<uint32_t *>(pm);
+            }
+    }
+
     // Clear the persistent path's step generation and tagged activations, so no
     // word left by a failed or timing launch can match a coming tag.
     void ds_reset()
@@ -840,6 +893,9 @@ struct ylm_engine
         cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
         cudaMemsetAsync(ds_xt, 0, sizeof(uint32_t) * H, st);
         cudaMemsetAsync(ds_actt, 0, sizeof(uint32_t) * inter, st);
+        for (uint32_t *m : ds_mb_local)
+            if (m)
+                cudaMemsetAsync(m, 0, sizeof(uint32_t) * tp * H, st);
     }
 
     // ModelBase::CalculateMaxSequenceLength (ModelBase.cpp:312-338)
@@ -908,6 +964,8 @@ struct ylm_engine
                 if (l < L)
                     CK(attn_decode_launch(attn_args(l), st, false));
             }
+            if (tp > 1)
+                NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
             if (sample)
                 CK(sample_launch(sample_args(), st, false));
             return;
@@ -1752,6 +1810,9 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
         if (!e || iters <= 0 || !ms_per_launch || !weight_bytes)
             fail(YLM_INVALID_ARG, "bad argument");
         if (!e->ds_on)
+            return (int)YLM_UNSUPPORTED;
+        // with tensor parallelism a segment waits on its peers' partials
+        if (e->tp > 1)
             return (int)YLM_UNSUPPORTED;
         if (layer < 0 || layer >= e->L)
             fail(YLM_INVALID_ARG, "layer out of range");

@@ -149,6 +149,8 @@ struct DsPhase
     const __half *bias;   // EPI_STORE bias or null
     uint32_t *resid_t;    // EPI_RESID target, the tagged residual stream; PRO_EMBED_RMSNORM: each
                           // CTA writes its rows of the embedding row here
+    int mbox;             // tensor parallel EPI_RESID: 0 none, 1 / 2 the mailbox set the partial
+                          // rows are all-reduced through (see DsArgs::mb)
 };
 #define DS_MAX_SEG_PHASES 4
 struct DsArgs
@@ -166,6 +168,11 @@ struct DsArgs
                         // a CTA's rows must not exceed the block size
     unsigned *gen;      // decode steps completed
     int *err;
+    // tensor parallelism: rank `rank` of `tp`; mb[s][q] is mailbox set s + 1 of
+    // rank q ([tp][hidden] tagged words, slot r written by rank r), mapped
+    // into this process (peer memory over NVLink for q != rank)
+    int tp, rank;
+    uint32_t *mb[2][8];
     int tab_bytes;  // shared-memory layout: phase table, work area, residual rows
     int work_bytes; // GEMV input vector, partials, RMSNorm scratch
     int kpad_max;   // largest input vector (halves, multiple of the task width)
