@@ -51,15 +51,31 @@
 
 namespace ylm {
 
-constexpr int DS_THREADS = 384; // 12 warps, one CTA per SM (168 registers per thread)
+#ifndef DS_U_OPT
+#define DS_U_OPT 8
+#endif
+#ifndef DS_D_OPT
+#define DS_D_OPT 3
+#endif
+#ifndef DS_THREADS_OPT
+#define DS_THREADS_OPT 384
+#endif
+constexpr int DS_THREADS = DS_THREADS_OPT; // 12 warps, one CTA per SM (168 registers per thread)
 constexpr int DS_WARPS = DS_THREADS / 32;
-constexpr int DS_U = 8;              // 16-byte vectors per lane per task
-constexpr int DS_KC = 32 * 8 * DS_U; // columns per task (2048)
-constexpr int DS_D = 3;              // register ring: DS_D - 1 tasks in flight per warp
+constexpr int DS_U = DS_U_OPT;       // 16-byte vectors per lane per task
+constexpr int DS_KC = 32 * 8 * DS_U; // columns per task
+constexpr int DS_D = DS_D_OPT;       // register ring: DS_D - 1 tasks in flight per warp
+static_assert(DS_U % 4 == 0, "four accumulators per lane");
 
+// This CTA's share of one GEMV phase, and the steps of a warp's task cursor
+// (tasks t = warp, warp + DS_WARPS, ...; task t is row r0 + t / nkc, chunk
+// t % nkc), so the task loop needs no division.
 struct DsTab
 {
-    int r0, rows, nkc, ntask; // this CTA's rows of one GEMV phase
+    const __half *w; // the phase's weights [N, K]
+    int K, nkc;      // columns, DS_KC-column chunks per row
+    int r0, rows;    // this CTA's rows
+    int drow, dkc;   // DS_WARPS tasks = drow rows + dkc chunks
 };
 
 __device__ __forceinline__ uint4 ds_ldg_stream(const void *p)
@@ -383,12 +399,56 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
     }
 }
 
+// Task cursor of one warp through the phases of a launch: phase, row, chunk,
+// task index (the partial's slot) and tasks left in the phase.
+struct DsCursor
+{
+    int ph, row, kc, t, left;
+};
+
+// Move `c` to the first task of this warp in phase c.ph or a later one.
+__device__ __forceinline__ void ds_cursor_enter(const DsTab *tab, int p0, int i1, int warp, DsCursor &c)
+{
+    for (; c.ph < i1; c.ph++)
+    {
+        const DsTab &tb = tab[c.ph - p0];
+        const int ntask = tb.rows * tb.nkc;
+        if (warp < ntask)
+        {
+            c.row = tb.r0 + warp / tb.nkc;
+            c.kc = warp % tb.nkc;
+            c.t = warp;
+            c.left = (ntask - warp + DS_WARPS - 1) / DS_WARPS;
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void ds_cursor_step(const DsTab *tab, int p0, int i1, int warp, DsCursor &c)
+{
+    if (--c.left == 0)
+    {
+        c.ph++;
+        ds_cursor_enter(tab, p0, i1, warp, c);
+        return;
+    }
+    const DsTab &tb = tab[c.ph - p0];
+    c.t += DS_WARPS;
+    c.row += tb.drow;
+    c.kc += tb.dkc;
+    if (c.kc >= tb.nkc)
+    {
+        c.kc -= tb.nkc;
+        c.row++;
+    }
+}
+
 // A run of consecutive GEMV phases [i0, i1). Each warp walks its task stream
-// (phase, task = warp, warp + 12, ...) with a ring of DS_D register buffers
-// whose roles are fixed by unrolling, so a buffer is never copied while its
-// loads are in flight; the first tasks of a phase are loaded while the
-// previous phase is still finishing.
-__device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsigned gen, int tid)
+// (phase, task = warp, warp + DS_WARPS, ...) with a ring of DS_D register
+// buffers whose roles are fixed by unrolling, so a buffer is never copied
+// while its loads are in flight; the first tasks of a phase are loaded while
+// the previous phase is still finishing.
+__device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsigned &gen, int tid)
 {
     const DsSmem sm = ds_smem_map(a);
     const DsTab *tab = sm.tab;
@@ -396,35 +456,26 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
     float *part = sm.part, *red = sm.red;
     __half *xr = sm.xr;
     const int warp = tid >> 5, lane = tid & 31;
-    int pp = i0, pt = warp; // prefetch cursor
-    while (pp < i1 && pt >= tab[pp - a.p0].ntask)
-    {
-        pp++;
-        pt = warp;
-    }
-    int cp = pp, ct = pt; // compute cursor
+    DsCursor pc{i0, 0, 0, 0, 0}; // loads
+    ds_cursor_enter(tab, a.p0, i1, warp, pc);
+    DsCursor cc = pc; // arithmetic
     uint4 buf[DS_D][DS_U];
     auto load = [&](uint4 *w) {
-        if (pp >= i1)
+        if (pc.ph >= i1)
             return;
-        const DsTab &t = tab[pp - a.p0];
-        const DsPhase &p = a.ph[pp - a.p0];
-        const int row = t.r0 + pt / t.nkc, kc = pt % t.nkc;
-        const __half *base = p.w + (size_t)row * p.K + kc * DS_KC + lane * 8;
-        const int lim = p.K - kc * DS_KC - lane * 8;
+        const DsTab &tb = tab[pc.ph - a.p0];
+        const __half *base = tb.w + (size_t)pc.row * tb.K + pc.kc * DS_KC + lane * 8;
+        const int lim = tb.K - pc.kc * DS_KC - lane * 8;
 #pragma unroll
         for (int u = 0; u < DS_U; u++)
             w[u] = u * 256 < lim ? ds_ldg_stream(base + u * 256) : make_uint4(0, 0, 0, 0);
-        pt += DS_WARPS;
-        while (pp < i1 && pt >= tab[pp - a.p0].ntask)
-        {
-            pp++;
-            pt = warp;
-        }
+        ds_cursor_step(tab, a.p0, i1, warp, pc);
     };
 #pragma unroll
     for (int d = 0; d < DS_D - 1; d++)
         load(buf[d]);
+    // the step generation (the tags) is read once the first weight loads are out
+    gen = *reinterpret_cast<volatile const unsigned *>(a.gen);
     // this CTA's rows of the residual stream, as the previous launch left them
     // (at most one per thread): loaded now, stored after the first prologue so
     // the two L2 round trips overlap (a layer-0 embedding prologue replaces them)
@@ -450,28 +501,22 @@ __device__ __forceinline__ void ds_segment(const DsArgs &a, int i0, int i1, unsi
 #pragma unroll
         for (int d = 0; d < DS_D; d++)
         {
-            while (cur < cp && cur < i1)
+            while (cur < cc.ph && cur < i1)
                 advance();
-            if (cp >= i1)
+            if (cc.ph >= i1)
                 goto done;
             load(buf[(d + DS_D - 1) % DS_D]);
             {
-                const DsTab &t = tab[cp - a.p0];
-                const int kc = ct % t.nkc;
-                const __half *xk = xs + kc * DS_KC + lane * 8;
-                float acc = 0.f;
+                // four interleaved accumulators (vectors u = j mod 4), as gemv_kernel
+                const __half *xk = xs + cc.kc * DS_KC + lane * 8;
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int u = 0; u < DS_U; u++)
-                    acc = ds_dot8(buf[d][u], *reinterpret_cast<const uint4 *>(xk + u * 256), acc);
-                acc = warp_sum(acc);
+                    acc[u & 3] = ds_dot8(buf[d][u], *reinterpret_cast<const uint4 *>(xk + u * 256), acc[u & 3]);
+                const float y = warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3]));
                 if (lane == 0)
-                    part[ct] = acc; // slot (row ct / nkc, chunk ct % nkc)
-                ct += DS_WARPS;
-                while (cp < i1 && ct >= tab[cp - a.p0].ntask)
-                {
-                    cp++;
-                    ct = warp;
-                }
+                    part[cc.t] = y; // slot (row t / nkc, chunk t % nkc)
+                ds_cursor_step(tab, a.p0, i1, warp, cc);
             }
         }
     }
@@ -486,7 +531,6 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
 {
     DsTab *tab = reinterpret_cast<DsTab *>(ds_smem);
     const int tid = threadIdx.x, C = gridDim.x, c = blockIdx.x;
-    const unsigned gen = *reinterpret_cast<volatile const unsigned *>(a.gen);
 
     for (int i = a.p0 + tid; i < a.p1; i += DS_THREADS)
     {
@@ -504,12 +548,16 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
             t.r0 = (int)((long long)p.N * c / C);
             t.rows = (int)((long long)p.N * (c + 1) / C) - t.r0;
         }
+        t.w = p.w;
+        t.K = p.K;
         t.nkc = (p.K + DS_KC - 1) / DS_KC;
-        t.ntask = t.rows * t.nkc;
+        t.drow = DS_WARPS / t.nkc;
+        t.dkc = DS_WARPS % t.nkc;
         tab[i - a.p0] = t;
     }
     __syncthreads();
 
+    unsigned gen = 0;
     ds_segment(a, a.p0, a.p1, gen, tid);
     // the step's last segment ends with a phase whose input is every CTA's
     // output of an earlier phase of this launch, so all CTAs have read *gen
@@ -521,6 +569,8 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_segment_kernel(const DsA
 int ds_threads() { return DS_THREADS; }
 
 int ds_task_cols() { return DS_KC; }
+
+int ds_tab_bytes() { return (int)((DS_MAX_SEG_PHASES * sizeof(DsTab) + 15) & ~(size_t)15); }
 
 cudaError_t ds_prepare(size_t smem, int *blocks_per_sm)
 {

@@ -803,7 +803,7 @@ struct ylm_engine
         for (size_t k = 0; k + 1 < cut.size(); k++)
             if (cut[k + 1] - cut[k] > DS_MAX_SEG_PHASES)
                 return;
-        const size_t tab_bytes = (size_t)DS_MAX_SEG_PHASES * 16;
+        const size_t tab_bytes = (size_t)ds_tab_bytes();
         const size_t work_bytes = ((size_t)kpad_max * 2 + (size_t)part_max * 4 + 32 * 4 + 15) & ~(size_t)15;
         const size_t xr_bytes = ((size_t)(H + C - 1) / C * 2 + 15) & ~(size_t)15;
         const size_t smem = tab_bytes + work_bytes + xr_bytes;

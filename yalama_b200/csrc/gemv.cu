@@ -15,9 +15,11 @@
 // Each CTA owns a contiguous block of rows; the block is cut into tasks of one
 // row x 2048 columns (4 KB), dealt round-robin to the CTA's eight warps. A warp
 // issues the 128-bit streaming loads (ld.global.nc, no L1 allocation) of its
-// next task before computing the current one, reduces each task with warp
-// shuffles into a per-(row, chunk) slot in shared memory, and the CTA sums the
-// slots in a fixed order for the epilogue, so results are bitwise reproducible.
+// next task before computing the current one (each lane keeps four FP32
+// accumulators, one per vector index mod 4, added pairwise at the end),
+// reduces each task with warp shuffles into a per-(row, chunk) slot in shared
+// memory, and the CTA sums the slots in a fixed order for the epilogue, so
+// results are bitwise reproducible.
 // Weights are constant, so the first task's loads are issued before
 // griddepcontrol.wait: under programmatic dependent launch they overlap the
 // tail of the previous kernel; x is read only after the wait.
@@ -38,6 +40,7 @@ constexpr int GV_THREADS = 256; // 8 warps
 constexpr int GV_WARPS = GV_THREADS / 32;
 constexpr int GV_U = 8;              // 16-byte vectors per lane per task
 constexpr int GV_KC = 32 * 8 * GV_U; // columns per task (2048)
+static_assert(GV_U % 4 == 0, "four accumulators per lane");
 constexpr int GV_CTAS_PER_SM = 2;
 constexpr int GV_PART_MAX = 4096;    // per-(row, chunk) partial slots per CTA
 
@@ -184,15 +187,17 @@ __global__ void __launch_bounds__(GV_THREADS, GV_CTAS_PER_SM) gemv_kernel(const 
         if (tn < ntask)
             gemv_load_task(p, r0 + tn / p.n_kc, tn % p.n_kc, lane, wnxt);
         const int kc = t % p.n_kc;
-        float acc = 0.f;
+        // four interleaved accumulators (vectors u = j mod 4): a shorter
+        // dependent FMA chain; the persistent decode path sums the same way
+        float a4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int u = 0; u < GV_U; u++)
         {
             float xv[8];
             unpack8(*reinterpret_cast<const uint4 *>(xs + kc * GV_KC + u * 256 + lane * 8), xv);
-            acc = dot8(wcur[u], xv, acc);
+            a4[u & 3] = dot8(wcur[u], xv, a4[u & 3]);
         }
-        acc = warp_sum(acc);
+        const float acc = warp_sum((a4[0] + a4[1]) + (a4[2] + a4[3]));
         if (lane == 0)
             part[t] = acc; // slot (row t / n_kc, chunk t % n_kc)
 #pragma unroll

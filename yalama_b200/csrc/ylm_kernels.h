@@ -180,6 +180,7 @@ struct DsArgs
 };
 int ds_threads();
 int ds_task_cols();
+int ds_tab_bytes(); // shared-memory bytes of a launch's phase table
 // Shared-memory opt-in and the resulting CTAs per SM.
 cudaError_t ds_prepare(size_t smem, int *blocks_per_sm);
 cudaError_t ds_launch(const DsArgs &a, size_t smem, int grid, cudaStream_t s);
