@@ -91,7 +91,7 @@ typedef struct ylm_engine_options {
     int32_t zero_kv_on_begin; /* 1 (default): BeginInfer zeroes the cache like ModelBase.cpp:302-309 */
     int32_t prefill_tensor_cores; /* 1 (default): tcgen05 GEMMs for prefill; 0: CUDA-core GEMMs */
     int32_t decode_persistent;    /* 1 (default): the projections between two attention launches of a
-                                     decode step run as one cooperative kernel; with tensor parallelism
+                                     decode step run as one persistent kernel; with tensor parallelism
                                      its O and down epilogues all-reduce over NVLink peer memory;
                                      0: the per-op graph */
 } ylm_engine_options;

@@ -302,7 +302,7 @@ struct ylm_engine
     // one argument block per segment (layer 0's QKV; O, gate-up, down and the
     // next QKV per layer; the last ends with the lm_head)
     bool ds_on = false;
-    bool ds_graph_ok = true; // cleared if the cooperative launches cannot be captured
+    bool ds_graph_ok = true; // cleared if the segment launches cannot be captured
     size_t ds_smem = 0;
     int ds_nph = 0;
     std::vector<DsPhase> ds_phases; // the step's GEMV phases (host copy)
@@ -729,18 +729,14 @@ struct ylm_engine
         dbg_probs = dalloc<float>(64);
     }
 
-    // Persistent GEMV segments: one cooperative launch (one CTA per SM) per run
-    // of projections between two attention launches, where the device can keep
+    // Persistent GEMV segments: one launch of one CTA per SM per run of
+    // projections between two attention launches, where the device can keep
     // one CTA per SM resident; otherwise the per-op graph. With tensor
     // parallelism the O and down epilogues all-reduce through peer mailboxes.
     void setup_persistent()
     {
         ds_on = false;
         if (!opt.decode_persistent || tp > 8)
-            return;
-        int coop = 0;
-        CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
-        if (!coop)
             return;
         ds_xt = dalloc<uint32_t>(H);
         ds_actt = dalloc<uint32_t>(inter);
@@ -1100,7 +1096,7 @@ struct ylm_engine
                 }
                 catch (...)
                 {
-                    // cooperative launches that do not capture: launch them directly
+                    // segment launches that do not capture: launch them directly
                     ds_graph_ok = false;
                     ex = nullptr;
                     cudaGetLastError();

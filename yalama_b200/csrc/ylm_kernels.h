@@ -133,7 +133,7 @@ cudaError_t sample_prepare();
 
 // ------------------------------------------------------------------ persistent GEMV segments
 // The projections between two attention launches of a decode step run as one
-// cooperative launch (decode_step.cu).
+// persistent launch of one CTA per SM (decode_step.cu).
 struct DsPhase
 {
     int pro;         // GemvPro
