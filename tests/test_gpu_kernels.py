@@ -71,6 +71,38 @@ def test_gemm_matches_fp32(t, n, k, tc):
     assert np.all(np.abs(got - ref) <= fp16_tol(ref, mag, k))
 
 
+@pytest.mark.parametrize("hq,hkv,t,cap", [(16, 8, 37, 64), (24, 8, 512, 600), (28, 4, 1000, 1000), (8, 8, 1, 16),
+                                           (64, 8, 130, 200), (4, 2, 65, 65), (32, 8, 2048, 2100)])
+def test_prefill_attention_matches_fp32(hq, hkv, t, cap):
+    # causal attention over cache slots [0, t); slots past t hold NaN, which
+    # must never reach the output (the reference never reads them either)
+    rng = np.random.default_rng(hq * 7 + t)
+    D = 128
+    q = rng.standard_normal((t, hq * D)).astype(np.float16)
+    kc = np.full((hkv, cap, D), np.nan, dtype=np.float16)
+    vc = np.full((hkv, cap, D), np.nan, dtype=np.float16)
+    kc[:, :t] = rng.standard_normal((hkv, t, D)).astype(np.float16)
+    vc[:, :t] = rng.standard_normal((hkv, t, D)).astype(np.float16)
+    qd, kd, vd = dev(q), dev(kc), dev(vc)
+    out = torch.empty((t, hq * D), dtype=torch.float16, device="cuda")
+    E.check(E.lib().ylm_k_prefill_attention(ptr(qd), ptr(kd), ptr(vd), cap, hq, hkv, t, ptr(out), stream()),
+            "prefill attention")
+    torch.cuda.synchronize()
+    qf = qd.float().reshape(t, hq, D).transpose(0, 1)                   # [hq, t, D]
+    kf = kd[:, :t].float().repeat_interleave(hq // hkv, dim=0)          # [hq, t, D]
+    vf = vd[:, :t].float().repeat_interleave(hq // hkv, dim=0)
+    sc = (qf @ kf.transpose(1, 2)) / np.sqrt(D)
+    mask = torch.triu(torch.ones(t, t, dtype=torch.bool, device="cuda"), 1)
+    sc = sc.masked_fill(mask, float("-inf"))
+    ref = (torch.softmax(sc, dim=-1) @ vf).transpose(0, 1).reshape(t, hq * D)
+    got = out.float()
+    assert torch.isfinite(got).all()
+    # P is rounded to FP16 before P V (one rounding per probability), and the
+    # output to FP16
+    err = (got - ref).abs().max().item()
+    assert err < 4e-3, err
+
+
 def rope_tables(max_pos, theta=1e6):
     half = 64
     inv = (1.0 / np.power(np.float64(np.float32(theta)), (np.arange(half, dtype=np.float32) / np.float32(half))

@@ -104,6 +104,18 @@ int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, vo
                                    static_cast<cudaStream_t>(stream)));
 }
 
+int ylm_k_prefill_attention(const void *q, const void *k_cache, const void *v_cache, int32_t cap, int32_t hq,
+                            int32_t hkv, int32_t t, void *out, void *stream)
+{
+    if (!q || !k_cache || !v_cache || !out || t <= 0 || t > cap || hkv <= 0 || hq <= 0 || hq % hkv)
+        return YLM_INVALID_ARG;
+    if (prepare_device() != cudaSuccess)
+        return YLM_CUDA_ERROR;
+    return cuda_status(attn_prefill_launch(static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
+                                           static_cast<const __half *>(v_cache), cap, hq, hkv, t,
+                                           static_cast<__half *>(out), static_cast<cudaStream_t>(stream)));
+}
+
 int ylm_k_decode_attention(const void *qkv, const void *q_norm, const void *k_norm, float eps, const void *rope_cos,
                            const void *rope_sin, int32_t max_pos, void *k_cache, void *v_cache, int32_t cap,
                            int32_t hq, int32_t hkv, int32_t slot, int32_t rope_pos, void *out, void *stream)

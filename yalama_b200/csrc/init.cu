@@ -91,6 +91,8 @@ cudaError_t kernels_prepare()
     if (e == cudaSuccess)
         e = attn_prepare();
     if (e == cudaSuccess)
+        e = attn_prefill_prepare();
+    if (e == cudaSuccess)
         e = sample_prepare();
     if (e == cudaSuccess)
         e = gemm_tc_prepare();

@@ -236,82 +236,241 @@ cudaError_t qkv_post_prefill_launch(const QkvPostArgs &a, cudaStream_t s)
 }
 
 // ------------------------------------------------------------------ causal attention
-// grid (ceil(T/32), hq), 4 warps, each warp 8 query rows. Keys in tiles of 32
-// from the KV cache (slots [0, T)); lane j scores key j of the tile.
-constexpr int AP_ROWS = 32, AP_KT = 32, AP_RPW = AP_ROWS / 4;
+// Flash attention on the tensor cores (mma.sync m16n8k16, FP16 inputs, FP32
+// accumulation). Replaces the prefill SDPA of ModelBase.cpp:671-693 with the
+// additive causal mask of :620-636 (implicit here) and without ExpandKV
+// (:695-707): query head h reads KV head h / (hq / hkv) straight from the cache.
+//
+// grid (ceil(T / 64), hq), 4 warps; warp w owns query rows r0 + 16 w .. + 15.
+// K and V tiles of 64 keys go through shared memory with cp.async, double
+// buffered; rows are 256 bytes and their 16-byte chunks are XOR-swizzled by
+// row & 7, so every ldmatrix phase reads eight distinct bank groups. The
+// scores stay in registers: the m16n8 accumulator of S = Q K^T is the A
+// fragment of P V after rounding P to FP16 (online softmax in FP32, base 2).
+// Rows past the prompt are zero-filled in shared memory (never read from the
+// cache), so a masked key never feeds a NaN into P V.
+constexpr int FA_BQ = 64, FA_BK = 64, FA_THREADS = 128;
+constexpr int FA_ROWB = YLM_HEAD_DIM * 2; // bytes per K / V / Q row
 
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const __half *q, const __half *kc, const __half *vc, int cap,
-                                                           int hq, int hkv, int T, __half *out)
+// byte offset of 16-byte chunk `chunk` of row `row` in a [rows][128] FP16 tile
+__device__ __forceinline__ uint32_t fa_swz(int row, int chunk)
 {
-    __shared__ float Kt[YLM_HEAD_DIM][AP_KT]; // transposed: Kt[d][key]
-    __shared__ float Vt[AP_KT][YLM_HEAD_DIM];
-    __shared__ float Qs[AP_ROWS][YLM_HEAD_DIM];
+    return (uint32_t)(row * FA_ROWB + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void fa_cp16(uint32_t dst, const void *src, bool valid)
+{
+    // src-size 0 writes 16 zero bytes and reads nothing
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fa_ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void fa_ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void fa_mma(float *d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t fa_pack(float lo, float hi)
+{
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(FA_THREADS) attn_prefill_kernel(const __half *q, const __half *kc, const __half *vc,
+                                                                  int cap, int hq, int hkv, int T, __half *out)
+{
+    extern __shared__ __align__(128) uint8_t fa_smem[];
+    // [Q 64 rows][K 2 x 64 rows][V 2 x 64 rows], each row 256 bytes
+    const uint32_t s_q = (uint32_t)__cvta_generic_to_shared(fa_smem);
+    const uint32_t s_k = s_q + FA_BQ * FA_ROWB;
+    const uint32_t s_v = s_k + 2 * FA_BK * FA_ROWB;
     const int h = blockIdx.y, g = h / (hq / hkv);
-    const int r0 = blockIdx.x * AP_ROWS;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float scale = 0.08838834764831845f * 1.4426950408889634f;
-    for (int i = threadIdx.x; i < AP_ROWS * YLM_HEAD_DIM; i += 128)
-    {
-        const int r = i / YLM_HEAD_DIM, d = i % YLM_HEAD_DIM;
-        Qs[r][d] = (r0 + r < T) ? h2f(q[(int64_t)(r0 + r) * hq * YLM_HEAD_DIM + h * YLM_HEAD_DIM + d]) * scale : 0.f;
-    }
-    float m[AP_RPW], l[AP_RPW], o[AP_RPW][4];
-    for (int i = 0; i < AP_RPW; i++)
-    {
-        m[i] = -INFINITY;
-        l[i] = 0.f;
-        for (int e = 0; e < 4; e++)
-            o[i][e] = 0.f;
-    }
-    const int last_row = min(T, r0 + AP_ROWS) - 1;
+    const int r0 = blockIdx.x * FA_BQ;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t qstride = (int64_t)hq * YLM_HEAD_DIM;
     const __half *kbase = kc + (int64_t)g * cap * YLM_HEAD_DIM;
     const __half *vbase = vc + (int64_t)g * cap * YLM_HEAD_DIM;
-    for (int k0 = 0; k0 <= last_row; k0 += AP_KT)
+
+    // Q tile: 16 chunks of 16 bytes per row
+    for (int i = tid; i < FA_BQ * 16; i += FA_THREADS)
     {
-        __syncthreads();
-        for (int i = threadIdx.x; i < AP_KT * YLM_HEAD_DIM; i += 128)
+        const int r = i >> 4, c = i & 15;
+        const bool ok = r0 + r < T;
+        fa_cp16(s_q + fa_swz(r, c), q + (ok ? (int64_t)(r0 + r) * qstride + h * YLM_HEAD_DIM + c * 8 : 0), ok);
+    }
+    const int last_row = min(T, r0 + FA_BQ) - 1;
+    const int ntiles = last_row / FA_BK + 1; // key tiles 0 .. the one holding the block's last row
+    auto load_kv = [&](int j, int buf) {
+        const int k0 = j * FA_BK;
+        for (int i = tid; i < FA_BK * 16; i += FA_THREADS)
         {
-            const int j = i % AP_KT, d = i / AP_KT;
-            Kt[d][j] = (k0 + j < T) ? h2f(kbase[(int64_t)(k0 + j) * YLM_HEAD_DIM + d]) : 0.f;
-            const int jv = i / YLM_HEAD_DIM, dv = i % YLM_HEAD_DIM;
-            Vt[jv][dv] = (k0 + jv < T) ? h2f(vbase[(int64_t)(k0 + jv) * YLM_HEAD_DIM + dv]) : 0.f;
+            const int r = i >> 4, c = i & 15;
+            const bool ok = k0 + r < T;
+            const int64_t off = ok ? (int64_t)(k0 + r) * YLM_HEAD_DIM + c * 8 : 0;
+            fa_cp16(s_k + buf * FA_BK * FA_ROWB + fa_swz(r, c), kbase + off, ok);
+            fa_cp16(s_v + buf * FA_BK * FA_ROWB + fa_swz(r, c), vbase + off, ok);
         }
-        __syncthreads();
-        for (int i = 0; i < AP_RPW; i++)
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_kv(0, 0); // (the Q copies join this group)
+
+    const int g4 = lane >> 2, c4 = lane & 3; // accumulator row / column pair of this lane
+    const int qr = warp * 16;                 // this warp's first row in the tile
+    const int row_a = r0 + qr + g4, row_b = row_a + 8;
+    const float sl2 = 0.08838834764831845f * 1.4426950408889634f; // 1/sqrt(128) * log2(e)
+    uint32_t qf[8][4];                                             // Q A-fragments, 8 steps of 16 dims
+    float o[16][4];                                                // O accumulators, 16 tiles of 8 dims
+#pragma unroll
+    for (int j = 0; j < 16; j++)
+        o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+
+    for (int j = 0; j < ntiles; j++)
+    {
+        const int buf = j & 1;
+        if (j + 1 < ntiles)
         {
-            const int row = r0 + warp * AP_RPW + i;
-            if (row >= T || k0 > row)
-                continue; // warp-uniform
-            float sc = 0.f;
-            for (int d = 0; d < YLM_HEAD_DIM; d++)
-                sc = fmaf(Qs[warp * AP_RPW + i][d], Kt[d][lane], sc);
-            const int key = k0 + lane;
-            if (key > row)
-                sc = -INFINITY;
-            const float mt = warp_max(sc);
-            const float mn = fmaxf(m[i], mt);
-            const float c = exp2f(m[i] - mn);
-            const float p = exp2f(sc - mn);
-            l[i] = l[i] * c + warp_sum(p);
-            for (int e = 0; e < 4; e++)
-                o[i][e] *= c;
-            for (int j = 0; j < AP_KT; j++)
+            load_kv(j + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        }
+        else
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        if (j == 0)
+        {
+            // x4 matrices: (rows 0-7, dims 0-7), (rows 8-15, dims 0-7), (rows 0-7, dims 8-15), (rows 8-15, dims 8-15)
+            const int mrow = qr + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++)
+                fa_ldsm_x4(s_q + fa_swz(mrow, kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        }
+        const uint32_t kb = s_k + buf * FA_BK * FA_ROWB, vb = s_v + buf * FA_BK * FA_ROWB;
+        // S = Q K^T: 8 tiles of 8 keys
+        float sc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; n++)
+            sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++)
+        {
+#pragma unroll
+            for (int n = 0; n < 8; n += 2)
             {
-                const float pj = __shfl_sync(0xffffffffu, p, j);
-                for (int e = 0; e < 4; e++)
-                    o[i][e] = fmaf(pj, Vt[j][lane * 4 + e], o[i][e]);
+                // matrices: (keys 8n.., dims 16kk..), (8n.., 16kk+8..), (8n+8.., 16kk..), (8n+8.., 16kk+8..)
+                const int krow = n * 8 + (lane & 7) + (lane >> 4) * 8;
+                const int kch = kk * 2 + ((lane >> 3) & 1);
+                uint32_t b0, b1, b2, b3;
+                fa_ldsm_x4(kb + fa_swz(krow, kch), b0, b1, b2, b3);
+                fa_mma(sc[n], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+                fa_mma(sc[n + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
             }
-            m[i] = mn;
         }
+        // scale, causal mask, online softmax (rows row_a and row_b, 4 lanes per row)
+        const int k0 = j * FA_BK;
+        float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < 8; n++)
+        {
+            const int key = k0 + n * 8 + c4 * 2;
+            sc[n][0] = key <= row_a ? sc[n][0] * sl2 : -INFINITY;
+            sc[n][1] = key + 1 <= row_a ? sc[n][1] * sl2 : -INFINITY;
+            sc[n][2] = key <= row_b ? sc[n][2] * sl2 : -INFINITY;
+            sc[n][3] = key + 1 <= row_b ? sc[n][3] * sl2 : -INFINITY;
+            mx_a = fmaxf(mx_a, fmaxf(sc[n][0], sc[n][1]));
+            mx_b = fmaxf(mx_b, fmaxf(sc[n][2], sc[n][3]));
+        }
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        // each tile holds key k0 <= every row of this block, so the maxima are finite
+        const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+        const float cr_a = exp2f(m_a - mn_a), cr_b = exp2f(m_b - mn_b);
+        m_a = mn_a;
+        m_b = mn_b;
+        float sum_a = 0.f, sum_b = 0.f;
+        uint32_t pf[4][4]; // P A-fragments, 4 steps of 16 keys
+#pragma unroll
+        for (int n = 0; n < 8; n++)
+        {
+            const float p0 = exp2f(sc[n][0] - mn_a), p1 = exp2f(sc[n][1] - mn_a);
+            const float p2 = exp2f(sc[n][2] - mn_b), p3 = exp2f(sc[n][3] - mn_b);
+            sum_a += p0 + p1;
+            sum_b += p2 + p3;
+            pf[n >> 1][(n & 1) * 2 + 0] = fa_pack(p0, p1);
+            pf[n >> 1][(n & 1) * 2 + 1] = fa_pack(p2, p3);
+        }
+        l_a = l_a * cr_a + sum_a;
+        l_b = l_b * cr_b + sum_b;
+#pragma unroll
+        for (int d = 0; d < 16; d++)
+        {
+            o[d][0] *= cr_a;
+            o[d][1] *= cr_a;
+            o[d][2] *= cr_b;
+            o[d][3] *= cr_b;
+        }
+        // O += P V: 4 steps of 16 keys x 16 tiles of 8 dims
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++)
+        {
+#pragma unroll
+            for (int d = 0; d < 16; d += 2)
+            {
+                // transposed: (keys 16kk.., dims 8d..), (16kk+8.., 8d..), (16kk.., 8d+8..), (16kk+8.., 8d+8..)
+                const int vrow = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int vch = d + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                fa_ldsm_x4_t(vb + fa_swz(vrow, vch), b0, b1, b2, b3);
+                fa_mma(o[d], pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3], b0, b1);
+                fa_mma(o[d + 1], pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3], b2, b3);
+            }
+        }
+        __syncthreads(); // this buffer is refilled by the next iteration's loads
     }
-    for (int i = 0; i < AP_RPW; i++)
+    // row sums over the 4 lanes of each row, then O / l
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+    const float inv_a = 1.f / l_a, inv_b = 1.f / l_b;
+#pragma unroll
+    for (int d = 0; d < 16; d++)
     {
-        const int row = r0 + warp * AP_RPW + i;
-        if (row >= T)
-            continue;
-        for (int e = 0; e < 4; e++)
-            out[(int64_t)row * hq * YLM_HEAD_DIM + h * YLM_HEAD_DIM + lane * 4 + e] = f2h(o[i][e] / l[i]);
+        const int col = h * YLM_HEAD_DIM + d * 8 + c4 * 2;
+        if (row_a < T)
+            *reinterpret_cast<__half2 *>(out + (int64_t)row_a * qstride + col) =
+                __floats2half2_rn(o[d][0] * inv_a, o[d][1] * inv_a);
+        if (row_b < T)
+            *reinterpret_cast<__half2 *>(out + (int64_t)row_b * qstride + col) =
+                __floats2half2_rn(o[d][2] * inv_b, o[d][3] * inv_b);
     }
+}
+
+static size_t fa_smem_bytes() { return (size_t)(FA_BQ + 4 * FA_BK) * FA_ROWB; }
+
+cudaError_t attn_prefill_prepare()
+{
+    return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)fa_smem_bytes());
 }
 
 cudaError_t attn_prefill_launch(const __half *q, const __half *k_cache, const __half *v_cache, int cap, int hq,
@@ -319,7 +478,10 @@ cudaError_t attn_prefill_launch(const __half *q, const __half *k_cache, const __
 {
     if (T <= 0)
         return cudaSuccess;
-    attn_prefill_kernel<<<dim3((T + AP_ROWS - 1) / AP_ROWS, hq), 128, 0, s>>>(q, k_cache, v_cache, cap, hq, hkv, T, out);
+    if (T > cap || hq % hkv)
+        return cudaErrorInvalidValue;
+    attn_prefill_kernel<<<dim3((T + FA_BQ - 1) / FA_BQ, hq), FA_THREADS, fa_smem_bytes(), s>>>(q, k_cache, v_cache,
+                                                                                              cap, hq, hkv, T, out);
     return cudaGetLastError();
 }
 
