@@ -176,6 +176,27 @@ def test_persistent_long_context_and_decode_loop():
     eg.close()
 
 
+@pytest.mark.parametrize("fam", sorted(FAMILIES))
+def test_prefill_gemm_epilogues_tensor_and_cuda_cores_agree(fam):
+    # 300 prompt rows: three 128-row GEMM tiles, the last one partial, through
+    # every epilogue (bias, residual add, SwiGLU) of both prefill GEMMs
+    spec, et = make(FAMILIES[fam], prefill_tensor_cores=1)
+    _, ec = make(FAMILIES[fam], prefill_tensor_cores=0)
+    orc = OracleModel(spec, synth.model_weights(spec, 0), mode="f16", kv_gb=2)
+    prompt = synth.prompt_ids(7, 300, spec.vocab)
+    out = []
+    for eng in (et, ec):
+        eng.begin_infer()
+        st, _ = eng.infer(prompt)
+        assert st == E.Status.OK
+        out.append(eng.logits())
+        eng.close()
+    orc.begin_infer()
+    _, lo = orc.infer(prompt)
+    assert np.max(np.abs(out[0] - out[1])) < LOGIT_TOL
+    assert np.max(np.abs(out[0] - lo)) < LOGIT_TOL
+
+
 def test_kv_capacity_rule_matches_reference():
     z = np.load(os.path.join(GOLDEN, "llama_kvcap.npz"))
     kw = json.loads(str(z["spec"]))

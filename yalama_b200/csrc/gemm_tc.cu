@@ -192,38 +192,92 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (row >= p.T || col0 >= p.N)
                     continue;
                 __half *crow = p.C + (int64_t)row * p.ldc;
+                // this thread's 32 columns are 64 contiguous bytes of its row:
+                // 16-byte accesses where the row start keeps them aligned
+                // (a warp's lanes are 32 different rows, so 2-byte accesses
+                // would cost one memory transaction per element)
+                const bool vec = col0 + 32 <= p.N && (p.ldc % 8) == 0;
                 if (p.epi == GEMM_SWIGLU)
                 {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 2)
+                    __half *dst = crow + (col0 >> 1);
+                    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0)
                     {
-                        const int col = col0 + j;
-                        if (col < p.N)
+                        uint4 pk[2];
+                        __half *hh = reinterpret_cast<__half *>(pk);
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
                         {
-                            const float g = rh(v[j]), u = rh(v[j + 1]);
+                            const float g = rh(v[2 * j]), u = rh(v[2 * j + 1]);
                             const float sg = rh(g / (1.0f + expf(-g)));
-                            crow[col >> 1] = f2h(sg * u);
+                            hh[j] = f2h(sg * u);
+                        }
+                        reinterpret_cast<uint4 *>(dst)[0] = pk[0];
+                        reinterpret_cast<uint4 *>(dst)[1] = pk[1];
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2)
+                        {
+                            const int col = col0 + j;
+                            if (col < p.N)
+                            {
+                                const float g = rh(v[j]), u = rh(v[j + 1]);
+                                const float sg = rh(g / (1.0f + expf(-g)));
+                                crow[col >> 1] = f2h(sg * u);
+                            }
                         }
                     }
                 }
                 else if (p.epi == GEMM_RESID)
                 {
+                    if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0)
+                    {
+                        uint4 *rp = reinterpret_cast<uint4 *>(crow + col0);
+                        uint4 r[4];
 #pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (col0 + j < p.N)
-                            crow[col0 + j] = f2h(h2f(crow[col0 + j]) + rh(v[j]));
+                        for (int j = 0; j < 4; j++)
+                            r[j] = rp[j];
+                        __half *rr = reinterpret_cast<__half *>(r);
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            rr[j] = f2h(h2f(rr[j]) + rh(v[j]));
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            rp[j] = r[j];
+                    }
+                    else
+                    {
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            if (col0 + j < p.N)
+                                crow[col0 + j] = f2h(h2f(crow[col0 + j]) + rh(v[j]));
+                    }
                 }
                 else
                 {
-                    // 16-byte stores only where the row start keeps them aligned (ldc % 8 == 0)
-                    if (col0 + 32 <= p.N && !p.bias && (p.ldc % 8) == 0 &&
-                        (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0)
+                    if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0 &&
+                        (!p.bias || (reinterpret_cast<uintptr_t>(p.bias + col0) & 15) == 0))
                     {
                         uint4 pk[4];
-                        __half2 *h = reinterpret_cast<__half2 *>(pk);
+                        __half *hh = reinterpret_cast<__half *>(pk);
+                        if (p.bias)
+                        {
+                            uint4 bq[4];
 #pragma unroll
-                        for (int j = 0; j < 16; j++)
-                            h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                            for (int j = 0; j < 4; j++)
+                                bq[j] = reinterpret_cast<const uint4 *>(p.bias + col0)[j];
+                            const __half *bb = reinterpret_cast<const __half *>(bq);
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                hh[j] = f2h(rh(v[j]) + h2f(bb[j]));
+                        }
+                        else
+                        {
+#pragma unroll
+                            for (int j = 0; j < 32; j++)
+                                hh[j] = f2h(v[j]);
+                        }
                         uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
 #pragma unroll
                         for (int j = 0; j < 4; j++)
