@@ -10,7 +10,8 @@
 //   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma
 //               (M=128, N=256, K=16, kind::f16, both operands K-major) and
 //               tcgen05.commit frees each stage and finally signals the epilogue
-//   warps 2-5   epilogue: tcgen05.ld of their 32-lane quadrant, 32 columns at a
+//   warps 2-9   epilogue: tcgen05.ld of their 32-lane quadrant (two warps per
+//               quadrant, each half of the 256 columns), 32 columns at a
 //               time, epilogue op, FP16 stores
 // Every wait is bounded; on expiry the kernel records an error, drains its own
 // copies and MMAs, releases TMEM and returns.
@@ -21,7 +22,8 @@
 namespace ylm {
 
 constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_ST = 4;
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 320; // producer, MMA issuer, 8 epilogue warps
+constexpr int TC_EPI_COLS = TC_BN / 2; // columns per epilogue warp
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2; // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2; // 32 KB
 constexpr int TC_TMEM_COLS = 256;
@@ -99,7 +101,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
+    // tiles in M-fastest order: the CTAs of a wave that share a W tile run
+    // together, so each W tile comes from HBM once and A stays in L2 (with N
+    // fastest, a W larger than L2 was re-read once per 128-row block)
+    const int mt = (p.T + TC_BM - 1) / TC_BM;
+    const int n0 = (int)(blockIdx.x / mt) * TC_BN, m0 = (int)(blockIdx.x % mt) * TC_BM;
     const int KT = (p.K + TC_BK - 1) / TC_BK;
 
     if (threadIdx.x == 0)
@@ -177,14 +183,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     else
     {
-        // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+        // epilogue warps 2..9 -> TMEM lane quadrant (warp % 4); warps 2-5 take
+        // columns [0, 128), warps 6-9 columns [128, 256)
         const int q = warp & 3;
+        const int cbeg = ((warp - 2) >> 2) * TC_EPI_COLS;
         const int row = m0 + q * 32 + lane;
         const bool ok = mbar_wait_bounded(accum, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
         tc_fence_after();
         if (ok && !*abort_flag)
         {
-            for (int c0 = 0; c0 < TC_BN; c0 += 32)
+            for (int c0 = cbeg; c0 < cbeg + TC_EPI_COLS; c0 += 32)
             {
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
@@ -367,7 +375,7 @@ cudaError_t gemm_tc_launch(const CUtensorMap &amap, const CUtensorMap &wmap, int
     a.C = C;
     a.ldc = ldc;
     a.err = err;
-    dim3 grid((N + TC_BN - 1) / TC_BN, (T + TC_BM - 1) / TC_BM);
+    dim3 grid((unsigned)(((N + TC_BN - 1) / TC_BN) * ((T + TC_BM - 1) / TC_BM)));
     gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(amap, wmap, a);
     return cudaGetLastError();
 }
