@@ -190,9 +190,10 @@ int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, vo
  * causal mask, src/models/ModelBase.cpp:620-636 and :671-693, without the GQA
  * ExpandKV copy of :695-707): q [t][hq*128] (RoPE applied), K/V already in the
  * cache at slots [0, t) of [hkv][cap][128]; out [t][hq*128]. FP16 inputs, FP32
- * accumulation, tensor cores. */
+ * accumulation. tensor_cores = 1: tcgen05 with TMEM accumulators (the engine's
+ * prefill); 0: mma.sync. */
 int ylm_k_prefill_attention(const void *q, const void *k_cache, const void *v_cache, int32_t cap, int32_t hq,
-                            int32_t hkv, int32_t t, void *out, void *stream);
+                            int32_t hkv, int32_t t, void *out, int32_t tensor_cores, void *stream);
 /* One decode-attention step for one layer: q/k-norm (optional), RoPE at rope_pos,
  * append k/v at `slot`, attention over slots [0, slot]. qkv: [(hq+2hkv)*128];
  * rope tables [max_pos][64]; caches [hkv][cap][128]; out [hq*128]. */

@@ -71,9 +71,11 @@ def test_gemm_matches_fp32(t, n, k, tc):
     assert np.all(np.abs(got - ref) <= fp16_tol(ref, mag, k))
 
 
+@pytest.mark.parametrize("tc", [1, 0])
 @pytest.mark.parametrize("hq,hkv,t,cap", [(16, 8, 37, 64), (24, 8, 512, 600), (28, 4, 1000, 1000), (8, 8, 1, 16),
-                                           (64, 8, 130, 200), (4, 2, 65, 65), (32, 8, 2048, 2100)])
-def test_prefill_attention_matches_fp32(hq, hkv, t, cap):
+                                           (64, 8, 130, 200), (4, 2, 65, 65), (32, 8, 2048, 2100),
+                                           (8, 2, 257, 300)])
+def test_prefill_attention_matches_fp32(hq, hkv, t, cap, tc):
     # causal attention over cache slots [0, t); slots past t hold NaN, which
     # must never reach the output (the reference never reads them either)
     rng = np.random.default_rng(hq * 7 + t)
@@ -85,7 +87,7 @@ def test_prefill_attention_matches_fp32(hq, hkv, t, cap):
     vc[:, :t] = rng.standard_normal((hkv, t, D)).astype(np.float16)
     qd, kd, vd = dev(q), dev(kc), dev(vc)
     out = torch.empty((t, hq * D), dtype=torch.float16, device="cuda")
-    E.check(E.lib().ylm_k_prefill_attention(ptr(qd), ptr(kd), ptr(vd), cap, hq, hkv, t, ptr(out), stream()),
+    E.check(E.lib().ylm_k_prefill_attention(ptr(qd), ptr(kd), ptr(vd), cap, hq, hkv, t, ptr(out), tc, stream()),
             "prefill attention")
     torch.cuda.synchronize()
     qf = qd.float().reshape(t, hq, D).transpose(0, 1)                   # [hq, t, D]

@@ -105,15 +105,18 @@ int ylm_k_gemm(const void *a, const void *w, int32_t t, int32_t n, int32_t k, vo
 }
 
 int ylm_k_prefill_attention(const void *q, const void *k_cache, const void *v_cache, int32_t cap, int32_t hq,
-                            int32_t hkv, int32_t t, void *out, void *stream)
+                            int32_t hkv, int32_t t, void *out, int32_t tensor_cores, void *stream)
 {
     if (!q || !k_cache || !v_cache || !out || t <= 0 || t > cap || hkv <= 0 || hq <= 0 || hq % hkv)
         return YLM_INVALID_ARG;
     if (prepare_device() != cudaSuccess)
         return YLM_CUDA_ERROR;
-    return cuda_status(attn_prefill_launch(static_cast<const __half *>(q), static_cast<const __half *>(k_cache),
-                                           static_cast<const __half *>(v_cache), cap, hq, hkv, t,
-                                           static_cast<__half *>(out), static_cast<cudaStream_t>(stream)));
+    const __half *qh = static_cast<const __half *>(q), *kh = static_cast<const __half *>(k_cache),
+                 *vh = static_cast<const __half *>(v_cache);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (tensor_cores)
+        return cuda_status(attn_prefill_tc_launch(qh, kh, vh, cap, hq, hkv, t, static_cast<__half *>(out), nullptr, s));
+    return cuda_status(attn_prefill_launch(qh, kh, vh, cap, hq, hkv, t, static_cast<__half *>(out), s));
 }
 
 int ylm_k_decode_attention(const void *qkv, const void *q_norm, const void *k_norm, float eps, const void *rope_cos,

@@ -1211,7 +1211,12 @@ struct ylm_engine
             q.T = T;
             q.pos0 = 0;
             CK(qkv_post_prefill_launch(q, st));
-            CK(attn_prefill_launch(pQ, kl, vl, cap, hq, hkv, T, pO, st));
+            // tcgen05 from 4096 tokens (measured 258 vs 253 TF/s at 8192); below,
+            // the mma.sync kernel is ahead (195 vs 176 TF/s at 2048)
+            if (opt.prefill_tensor_cores && T >= 4096)
+                CK(attn_prefill_tc_launch(pQ, kl, vl, cap, hq, hkv, T, pO, &dstate->err, st));
+            else
+                CK(attn_prefill_launch(pQ, kl, vl, cap, hq, hkv, T, pO, st));
             if (tp == 1)
                 pgemm(pO, m_o, hq * D, y.wo, y.to, T, H, hq * D, GEMM_RESID, nullptr, pX, H);
             else

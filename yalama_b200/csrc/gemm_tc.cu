@@ -87,6 +87,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v)
         v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v)
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+                 "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+                 "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+                 "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+                 "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+                 "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+                 "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+                 "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+                 "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+                 "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+                 : "memory");
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const TcArgs p)
 {
@@ -316,6 +334,315 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------ prefill attention (tcgen05)
+// Causal flash attention of a prompt on the 5th-generation tensor cores: the
+// prefill SDPA of ModelBase.cpp:671-693 with the causal mask of :620-636
+// (implicit) and no ExpandKV (:695-707): query head h reads KV head h / G from
+// the cache. One CTA per 128 query rows of one head, 6 warps:
+//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys (two
+//               stages) from 3-D tensor maps whose key extent is the prompt
+//               length, so keys past it arrive as zeros
+//   warp 1      one thread issues S = Q K^T (M=128, N=128, K=128, both K-major)
+//               into TMEM columns [0, 128), then O += P V into [128, 256)
+//               (P K-major from shared memory, V MN-major: the tile as stored)
+//   warps 2-5   one query row per thread (its TMEM lane): scale, causal mask,
+//               running max, P = exp2(s - m) rounded to FP16 into shared memory
+//               in the 128-byte-swizzled K-major layout; O accumulates in TMEM
+//               across tiles and is rescaled in place (tcgen05.ld / st) before
+//               the next P V whenever a row's maximum grew
+// All waits are bounded; a timeout records YLM_DEV_ERR_TIMEOUT_* and unwinds.
+constexpr int FT_BM = 128, FT_BN = 128, FT_THREADS = 192;
+constexpr int FT_TILE = 128 * 128 * 2; // one 128 x 128 FP16 tile: two 64-column atoms of 16 KB
+constexpr int FT_TMEM_COLS = 256;
+constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * 6 + 256; // Q, K x2, V x2, P + barriers
+
+// MN-major operand tile with the 128-byte swizzle: 64-element rows along MN,
+// `lbo` bytes between 64-element MN blocks, `sbo` bytes between 8-row K groups.
+__device__ __forceinline__ uint64_t smem_desc_mn128(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+struct FtArgs
+{
+    int T, hq, hkv;
+    __half *out; // [T][hq * 128]
+    int *err;
+};
+
+__global__ void __launch_bounds__(FT_THREADS, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, const FtArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *sq = smem;
+    uint8_t *sk = sq + FT_TILE;         // 2 stages
+    uint8_t *sv = sk + 2 * FT_TILE;     // 2 stages
+    uint8_t *sp = sv + 2 * FT_TILE;     // P
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sp + FT_TILE);
+    uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 6,
+             *o_full = bars + 7, *done = bars + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 10);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qb = blockIdx.x, h = blockIdx.y, g = h / (p.hq / p.hkv);
+    const int r0 = qb * FT_BM;
+    const int nt = qb + 1; // key tiles 0 .. the diagonal one
+
+    if (threadIdx.x == 0)
+    {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; s++)
+        {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(o_full, 1);
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(FT_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            prefetch_tensormap(&qmap);
+            prefetch_tensormap(&kmap);
+            prefetch_tensormap(&vmap);
+            mbar_arrive_expect_tx(q_full, FT_TILE);
+            tma_load_2d(sq, &qmap, h * 128, r0, q_full);
+            tma_load_2d(sq + FT_TILE / 2, &qmap, h * 128 + 64, r0, q_full);
+            int issued = 0;
+            for (int j = 0; j < nt; j++)
+            {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                {
+                    *abort_flag = 1;
+                    break;
+                }
+                if (*abort_flag)
+                    break;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * FT_TILE);
+                tma_load_3d(sk + s * FT_TILE, &kmap, 0, j * FT_BN, g, &kv_full[s]);
+                tma_load_3d(sk + s * FT_TILE + FT_TILE / 2, &kmap, 64, j * FT_BN, g, &kv_full[s]);
+                tma_load_3d(sv + s * FT_TILE, &vmap, 0, j * FT_BN, g, &kv_full[s]);
+                tma_load_3d(sv + s * FT_TILE + FT_TILE / 2, &vmap, 64, j * FT_BN, g, &kv_full[s]);
+                issued++;
+            }
+            // every issued copy has landed before the CTA can exit
+            mbar_wait_bounded(q_full, 0, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+            for (int j = issued > 2 ? issued - 2 : 0; j < issued; j++)
+                mbar_wait_bounded(&kv_full[j & 1], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            const uint32_t idesc_s = tc_idesc(FT_BM, FT_BN);
+            const uint32_t idesc_o = tc_idesc(FT_BM, 128) | (1u << 16); // B (V) MN-major
+            bool ok = mbar_wait_bounded(q_full, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
+            const uint32_t q0 = smem_u32(sq), pb = smem_u32(sp);
+            for (int j = 0; ok && j < nt; j++)
+            {
+                const int s = j & 1;
+                if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t k0 = smem_u32(sk + s * FT_TILE), v0 = smem_u32(sv + s * FT_TILE);
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++)
+                {
+                    const uint32_t off = (uint32_t)((kk >> 2) * (FT_TILE / 2) + (kk & 3) * 32);
+                    tc_mma(tmem, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), idesc_s, kk ? 1u : 0u);
+                }
+                tc_commit(s_full);
+                if (!mbar_wait_bounded(p_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++)
+                {
+                    const uint32_t poff = (uint32_t)((kk >> 2) * (FT_TILE / 2) + (kk & 3) * 32);
+                    tc_mma(tmem + 128, smem_desc_k128(pb + poff), smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024),
+                           idesc_o, (j | kk) ? 1u : 0u);
+                }
+                tc_commit(o_full);
+                tc_commit(&kv_empty[s]);
+            }
+            if (!ok)
+                *abort_flag = 1;
+            // all issued MMAs complete before TMEM is released
+            tc_commit(done);
+            mbar_wait_bounded(done, 0, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    }
+    else
+    {
+        const int q = warp & 3;           // TMEM lane quadrant of this warp
+        const int row = q * 32 + lane;    // query row in the tile
+        const int grow = r0 + row;
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+        const float sl2 = 0.08838834764831845f * 1.4426950408889634f; // 1/sqrt(128) * log2(e)
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nt; j++)
+        {
+            // (every wait ends in a warp-wide vote: the TMEM accesses below are
+            // warp-collective, so the lanes leave together or not at all)
+            const bool sw = mbar_wait_bounded(s_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
+            if (!__all_sync(0xffffffffu, sw))
+            {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int key0 = j * FT_BN;
+            // pass 1: the row maximum of this tile (masked keys excluded)
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c0 = 0; c0 < 128; c0 += 32)
+            {
+                float v[32];
+                tmem_ld32(trow + (uint32_t)c0, v);
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (key0 + c0 + i <= grow)
+                        mx = fmaxf(mx, v[i] * sl2);
+            }
+            // each tile holds key j*128 <= every row of this block: mx is finite
+            const float mn = fmaxf(m, mx);
+            const float corr = exp2f(m - mn);
+            m = mn;
+            // the previous P V has finished (P and the O columns are free):
+            // rescale this row of O unless no row of the warp changed its maximum
+            if (j > 0)
+            {
+                if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_full, (j - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL)))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (!__all_sync(0xffffffffu, corr == 1.f))
+                {
+#pragma unroll
+                    for (int c0 = 0; c0 < 128; c0 += 32)
+                    {
+                        float v[32];
+                        tmem_ld32(trow + 128u + (uint32_t)c0, v);
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            v[i] *= corr;
+                        tmem_st32(trow + 128u + (uint32_t)c0, v);
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                }
+            }
+            // pass 2: P = exp2(s - m) in FP16, 16-byte chunks into the swizzled layout
+            float sum = 0.f;
+#pragma unroll
+            for (int c0 = 0; c0 < 128; c0 += 32)
+            {
+                float v[32];
+                tmem_ld32(trow + (uint32_t)c0, v);
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2)
+                {
+                    const float p0 = key0 + c0 + i <= grow ? exp2f(v[i] * sl2 - mn) : 0.f;
+                    const float p1 = key0 + c0 + i + 1 <= grow ? exp2f(v[i + 1] * sl2 - mn) : 0.f;
+                    sum += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&hp);
+                }
+#pragma unroll
+                for (int ch = 0; ch < 4; ch++)
+                {
+                    const int c = (c0 >> 3) + ch; // 16-byte chunk of the row: keys 8c .. 8c + 7
+                    uint8_t *dst = sp + (c >> 3) * (FT_TILE / 2) + row * 128 + (((c & 7) ^ (row & 7)) << 4);
+                    *reinterpret_cast<uint4 *>(dst) =
+                        make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+                }
+            }
+            l = l * corr + sum;
+            // P visible to the tensor cores; this thread's TMEM reads and writes done
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        const bool fw = ok && mbar_wait_bounded(o_full, (nt - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
+        if (__all_sync(0xffffffffu, fw))
+        {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            __half *dst = p.out + (int64_t)grow * p.hq * 128 + h * 128;
+#pragma unroll
+            for (int c0 = 0; c0 < 128; c0 += 32)
+            {
+                float v[32];
+                tmem_ld32(trow + 128u + (uint32_t)c0, v);
+                if (grow < p.T)
+                {
+#pragma unroll
+                    for (int c8 = 0; c8 < 32; c8 += 8)
+                    {
+                        uint4 pk;
+                        __half2 *hh = reinterpret_cast<__half2 *>(&pk);
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            hh[i] = __floats2half2_rn(v[c8 + 2 * i] * inv, v[c8 + 2 * i + 1] * inv);
+                        *reinterpret_cast<uint4 *>(dst + c0 + c8) = pk;
+                    }
+                }
+            }
+        }
+        else
+            *abort_flag = 1;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FT_TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 encoder()
 {
@@ -377,6 +704,63 @@ cudaError_t gemm_tc_launch(const CUtensorMap &amap, const CUtensorMap &wmap, int
     a.err = err;
     dim3 grid((unsigned)(((N + TC_BN - 1) / TC_BN) * ((T + TC_BM - 1) / TC_BM)));
     gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(amap, wmap, a);
+    return cudaGetLastError();
+}
+
+
+// Tensor maps of the prefill attention: Q [T][hq*128] in 64 x 128 boxes; K and
+// V of one layer as [hkv][T of cap][128] in 64 x 128 x 1 boxes (the key extent
+// is T, so rows past the prompt are filled with zeros).
+static bool ft_make_maps(CUtensorMap *qm, CUtensorMap *km, CUtensorMap *vm, const __half *q, const __half *k,
+                         const __half *v, int cap, int hq, int hkv, int T)
+{
+    auto enc = encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) % 16)
+        return false;
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)hq * 128, (cuuint64_t)T};
+        cuuint64_t strides[1] = {(cuuint64_t)hq * 128 * 2};
+        cuuint32_t box[2] = {64, 128};
+        cuuint32_t estr[2] = {1, 1};
+        if (enc(qm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(q), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    cuuint64_t dims[3] = {128, (cuuint64_t)T, (cuuint64_t)hkv};
+    cuuint64_t strides[2] = {256, (cuuint64_t)cap * 256};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    for (int i = 0; i < 2; i++)
+        if (enc(i ? vm : km, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(i ? v : k), dims, strides, box,
+                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    return true;
+}
+
+cudaError_t attn_prefill_tc_prepare()
+{
+    return cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FT_SMEM);
+}
+
+cudaError_t attn_prefill_tc_launch(const __half *q, const __half *k_cache, const __half *v_cache, int cap, int hq,
+                                   int hkv, int T, __half *out, int *err, cudaStream_t s)
+{
+    if (T <= 0)
+        return cudaSuccess;
+    if (T > cap || hkv <= 0 || hq % hkv)
+        return cudaErrorInvalidValue;
+    CUtensorMap qm, km, vm;
+    if (!ft_make_maps(&qm, &km, &vm, q, k_cache, v_cache, cap, hq, hkv, T))
+        return cudaErrorNotSupported;
+    FtArgs a;
+    a.T = T;
+    a.hq = hq;
+    a.hkv = hkv;
+    a.out = out;
+    a.err = err;
+    attn_prefill_tc_kernel<<<dim3((T + FT_BM - 1) / FT_BM, hq), FT_THREADS, FT_SMEM, s>>>(qm, km, vm, a);
     return cudaGetLastError();
 }
 

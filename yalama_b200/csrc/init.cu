@@ -93,6 +93,8 @@ cudaError_t kernels_prepare()
     if (e == cudaSuccess)
         e = attn_prefill_prepare();
     if (e == cudaSuccess)
+        e = attn_prefill_tc_prepare();
+    if (e == cudaSuccess)
         e = sample_prepare();
     if (e == cudaSuccess)
         e = gemm_tc_prepare();

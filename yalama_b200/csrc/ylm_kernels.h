@@ -229,6 +229,10 @@ cudaError_t qkv_post_prefill_launch(const QkvPostArgs &a, cudaStream_t s);
 cudaError_t resid_add_rows_launch(__half *x, const __half *y, int64_t n, cudaStream_t s);
 // causal attention over KV slots [0, T): q [T][hq*128] -> out [T][hq*128]
 cudaError_t attn_prefill_prepare();
+// The same on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
+cudaError_t attn_prefill_tc_prepare();
+cudaError_t attn_prefill_tc_launch(const __half *q, const __half *k_cache, const __half *v_cache, int cap, int hq,
+                                   int hkv, int T, __half *out, int *err, cudaStream_t s);
 cudaError_t attn_prefill_launch(const __half *q, const __half *k_cache, const __half *v_cache, int cap, int hq,
                                 int hkv, int T, __half *out, cudaStream_t s);
 

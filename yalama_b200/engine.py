@@ -146,7 +146,7 @@ SIGNATURES = {
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
     "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_prefill_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
-                                               ctypes.c_int32, _P, _P]),
+                                               ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_decode_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_float, _P, _P, ctypes.c_int32, _P, _P,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, _P, _P]),
