@@ -1211,9 +1211,9 @@ struct ylm_engine
             q.T = T;
             q.pos0 = 0;
             CK(qkv_post_prefill_launch(q, st));
-            // tcgen05 from 4096 tokens (measured 258 vs 253 TF/s at 8192); below,
-            // the mma.sync kernel is ahead (195 vs 176 TF/s at 2048)
-            if (opt.prefill_tensor_cores && T >= 4096)
+            // tcgen05 (measured 327 / 229 TF/s at 8192 / 2048 tokens against
+            // 252 / 195 for the mma.sync kernel, which prefill_tensor_cores = 0 selects)
+            if (opt.prefill_tensor_cores)
                 CK(attn_prefill_tc_launch(pQ, kl, vl, cap, hq, hkv, T, pO, &dstate->err, st));
             else
                 CK(attn_prefill_launch(pQ, kl, vl, cap, hq, hkv, T, pO, st));

@@ -338,23 +338,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // Causal flash attention of a prompt on the 5th-generation tensor cores: the
 // prefill SDPA of ModelBase.cpp:671-693 with the causal mask of :620-636
 // (implicit) and no ExpandKV (:695-707): query head h reads KV head h / G from
-// the cache. One CTA per 128 query rows of one head, 6 warps:
+// the cache. One CTA per 128 query rows of one head, 10 warps:
 //   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys (two
 //               stages) from 3-D tensor maps whose key extent is the prompt
 //               length, so keys past it arrive as zeros
 //   warp 1      one thread issues S = Q K^T (M=128, N=128, K=128, both K-major)
 //               into TMEM columns [0, 128), then O += P V into [128, 256)
 //               (P K-major from shared memory, V MN-major: the tile as stored)
-//   warps 2-5   one query row per thread (its TMEM lane): scale, causal mask,
+//   warps 2-9   one query row per two threads (their TMEM lane; 64 of the
+//               row's columns each, maxima and sums exchanged through shared
+//               memory): scale, causal mask,
 //               running max, P = exp2(s - m) rounded to FP16 into shared memory
 //               in the 128-byte-swizzled K-major layout; O accumulates in TMEM
 //               across tiles and is rescaled in place (tcgen05.ld / st) before
 //               the next P V whenever a row's maximum grew
 // All waits are bounded; a timeout records YLM_DEV_ERR_TIMEOUT_* and unwinds.
-constexpr int FT_BM = 128, FT_BN = 128, FT_THREADS = 192;
+constexpr int FT_BM = 128, FT_BN = 128, FT_THREADS = 320; // TMA, MMA, 8 softmax warps
 constexpr int FT_TILE = 128 * 128 * 2; // one 128 x 128 FP16 tile: two 64-column atoms of 16 KB
 constexpr int FT_TMEM_COLS = 256;
-constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * 6 + 256; // Q, K x2, V x2, P + barriers
+constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * 6 + 256 + 2 * 2 * 128 * 4; // Q, K x2, V x2, P, barriers, row exchange
 
 // MN-major operand tile with the 128-byte swizzle: 64-element rows along MN,
 // `lbo` bytes between 64-element MN blocks, `sbo` bytes between 8-row K groups.
@@ -395,6 +397,9 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
              *o_full = bars + 7, *done = bars + 8;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 10);
+    uint64_t *xbar = bars + 11; // row exchange between the two softmax halves (256 arrivals)
+    float *xrow = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256); // maxima [2 halves][128 rows]
+    float *xsum = xrow + 256;                                                          // sums [2][128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qb = blockIdx.x, h = blockIdx.y, g = h / (p.hq / p.hkv);
@@ -410,7 +415,8 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             mbar_init(&kv_empty[s], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(p_full, 128);
+        mbar_init(p_full, 256);
+        mbar_init(xbar, 256);
         mbar_init(o_full, 1);
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -514,9 +520,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     else
     {
         const int q = warp & 3;           // TMEM lane quadrant of this warp
+        const int hf = (warp - 2) >> 2;   // which 64 of the row's 128 keys / dims (warps 2-5: 0, 6-9: 1)
         const int row = q * 32 + lane;    // query row in the tile
         const int grow = r0 + row;
         const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+        const int cb = hf * 64;           // this thread's columns [cb, cb + 64)
         const float sl2 = 0.08838834764831845f * 1.4426950408889634f; // 1/sqrt(128) * log2(e)
         float m = -INFINITY, l = 0.f;
         bool ok = true;
@@ -535,7 +543,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             // pass 1: the row maximum of this tile (masked keys excluded)
             float mx = -INFINITY;
 #pragma unroll
-            for (int c0 = 0; c0 < 128; c0 += 32)
+            for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
                 tmem_ld32(trow + (uint32_t)c0, v);
@@ -544,6 +552,17 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     if (key0 + c0 + i <= grow)
                         mx = fmaxf(mx, v[i] * sl2);
             }
+            // the row's other half, through shared memory (a thread writes the
+            // next tile's value only after both halves arrived on p_full for
+            // this one, so the partner has read it); phase j of xbar
+            xrow[hf * 128 + row] = mx;
+            mbar_arrive(xbar);
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL)))
+            {
+                ok = false;
+                break;
+            }
+            mx = fmaxf(mx, xrow[(hf ^ 1) * 128 + row]);
             // each tile holds key j*128 <= every row of this block: mx is finite
             const float mn = fmaxf(m, mx);
             const float corr = exp2f(m - mn);
@@ -561,7 +580,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 if (!__all_sync(0xffffffffu, corr == 1.f))
                 {
 #pragma unroll
-                    for (int c0 = 0; c0 < 128; c0 += 32)
+                    for (int c0 = cb; c0 < cb + 64; c0 += 32)
                     {
                         float v[32];
                         tmem_ld32(trow + 128u + (uint32_t)c0, v);
@@ -576,7 +595,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             // pass 2: P = exp2(s - m) in FP16, 16-byte chunks into the swizzled layout
             float sum = 0.f;
 #pragma unroll
-            for (int c0 = 0; c0 < 128; c0 += 32)
+            for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
                 tmem_ld32(trow + (uint32_t)c0, v);
@@ -605,14 +624,23 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             tc_fence_before();
             mbar_arrive(p_full);
         }
-        const bool fw = ok && mbar_wait_bounded(o_full, (nt - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
+        // the row sum over both halves: phase nt of xbar
+        bool fw = ok;
+        if (fw)
+        {
+            xsum[hf * 128 + row] = l;
+            mbar_arrive(xbar);
+            fw = mbar_wait_bounded(xbar, nt & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
+            l += xsum[(hf ^ 1) * 128 + row];
+        }
+        fw = fw && mbar_wait_bounded(o_full, (nt - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
         if (__all_sync(0xffffffffu, fw))
         {
             tc_fence_after();
             const float inv = 1.f / l;
             __half *dst = p.out + (int64_t)grow * p.hq * 128 + h * 128;
 #pragma unroll
-            for (int c0 = 0; c0 < 128; c0 += 32)
+            for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
                 tmem_ld32(trow + 128u + (uint32_t)c0, v);
