@@ -1883,6 +1883,13 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
         cudaEvent_t a, b;
         CK(cudaEventCreate(&a));
         CK(cudaEventCreate(&b));
+        // with tensor parallelism the ranks' host threads reach this point at
+        // different times; a one-element all-reduce lines their streams up, so
+        // the timed steps start together instead of the earliest rank's first
+        // step absorbing the others' host lag (its segments wait for their
+        // partials)
+        if (e->tp > 1)
+            NK(ncclAllReduce(e->ar, e->ar, 1, ncclHalf, ncclSum, e->comm, e->st));
         CK(cudaEventRecord(a, e->st));
         for (int i = 0; i < iters; i++)
             e->launch_forward(true);
