@@ -1,14 +1,14 @@
 #!/usr/bin/env python
 """Batch-1 FP16 decode benchmark of the yalama B200 engine.
 
-Workload (one "step" = one request): a Llama-3.2-3B-shaped FP16 model
-(hidden 3072, 28 layers, 24 Q / 8 KV heads, head_dim 128, intermediate 8192,
-vocab 128256, tied embeddings), random-init N(0, 0.02) weights from a seed,
-a 512-token uniform-random prompt, then 256 generated tokens with top-k 40 and
-temperature 0.6 (the first token greedy, as the reference's token loop does).
-Synthetic data: no checkpoint or dataset is read.
+Default workload (one "step" = one request): a Llama-3.1-8B-shaped FP16 model
+(hidden 4096, 32 layers, 32 Q / 8 KV heads, head_dim 128, intermediate 14336,
+vocab 128256, untied lm_head), random-init N(0, 0.02) weights from a seed, a
+2048-token uniform-random prompt, then 1024 greedily generated tokens. Other
+shapes run with ``--workload`` (see WORKLOADS). Synthetic data: no checkpoint or
+dataset is read.
 
-  value   decode tok/s with everything resident in HBM: the 255 decode steps of
+  value   decode tok/s with everything resident in HBM: the 1023 decode steps of
           each request run as back-to-back CUDA-graph launches (one graph per
           token: the whole forward + on-device sampling), timed with CUDA events
           on the engine stream; max over ranks.
@@ -18,10 +18,12 @@ Synthetic data: no checkpoint or dataset is read.
           ((generated - 1) / sum of per-token times).
 
 At N > 1 the model is tensor-parallel over the N GPUs of the node (strong
-scaling: the same request, split). Weights (6.4 GB) far exceed the 126 MB L2,
-so no flush is needed between timed steps.
+scaling: the same request, split), and the line carries the per-token time
+spent in the all-reduce exchanges. Weights (16 GB) far exceed the 126 MB L2, so
+no flush is needed between timed steps. At N = 1 the line also carries the
+Llama-3.2-3B top-k 40 / temperature 0.6 workload as an extra key.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload NAME]
 """
 from __future__ import annotations
 
@@ -29,6 +31,7 @@ import argparse
 import ctypes
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -38,11 +41,24 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-WORKLOAD = {"preset": "llama3.2-3b", "prompt": 512, "decode": 256, "top_k": 40, "temperature": 0.6,
-            "weight_seed": 0, "prompt_seed": 0, "sample_seed": 1234}
+# name -> (model preset, prompt tokens, generated tokens, top_k (0 = greedy), temperature)
+WORKLOADS = {
+    "llama3.1-8b": ("llama3.1-8b", 2048, 1024, 0, 0.6),
+    "llama3.2-3b": ("llama3.2-3b", 512, 256, 40, 0.6),
+    "qwen3-0.6b": ("qwen3-0.6b", 32, 128, 0, 0.6),
+    "qwen2.5-7b": ("qwen2.5-7b", 8192, 512, 0, 0.6),
+    "mistral-7b-v0.3": ("mistral-7b-v0.3", 2048, 1024, 0, 0.6),
+    "llama3.1-70b": ("llama3.1-70b", 4096, 512, 0, 0.6),
+}
+DEFAULT_WORKLOAD = "llama3.1-8b"
+EXTRA_WORKLOAD = "llama3.2-3b"
+SEEDS = {"weight_seed": 0, "prompt_seed": 0, "sample_seed": 1234}
 METRIC = "batch-1 FP16 decode tok/s"
+# the CPU reference runs a bounded sample: this many prompt tokens at most, then a few decode tokens
+CPU_SAMPLE_PROMPT = 128
 REF_CPU = os.path.join(ROOT, "oracle", "_ref", "ref_cpu_f32")
 REF_GPU = os.path.join(ROOT, "oracle", "_ref", "ref_gpu_f16")
+REF_GPU_BF16 = os.path.join(ROOT, "oracle", "_ref", "ref_gpu_bf16")
 
 
 def peaks():
@@ -119,36 +135,79 @@ def args_():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--preset", default=WORKLOAD["preset"])
-    ap.add_argument("--prompt", type=int, default=WORKLOAD["prompt"])
-    ap.add_argument("--decode", type=int, default=WORKLOAD["decode"])
+    ap.add_argument("--workload", "--preset", dest="workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--prompt", type=int, default=0, help="override the workload's prompt length")
+    ap.add_argument("--decode", type=int, default=0, help="override the workload's generated tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the extra top-k workload at N = 1")
     ap.add_argument("--e2e-requests", type=int, default=2)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for profiler captures; not a bench number)")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--decode-path", default="persistent", choices=["persistent", "per-op"],
                     help="persistent GEMV segments (default) or the per-op graph")
-    return ap.parse_args()
+    a = ap.parse_args()
+    preset, prompt, decode, top_k, temp = WORKLOADS[a.workload]
+    a.preset = preset
+    a.prompt = a.prompt or prompt
+    a.decode = a.decode or decode
+    a.top_k, a.temperature = top_k, temp
+    return a
 
 
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def sampling_desc(top_k, temp):
+    return "greedy" if top_k == 0 else f"top-k {top_k}, temperature {temp} (first token greedy)"
+
+
+# ---------------------------------------------------------------- host resources
+def host_mem_available():
+    try:
+        for line in open("/proc/meminfo"):
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return None
+
+
+def scratch_dir(need_bytes):
+    """A folder with room for a snapshot of `need_bytes` (RAM-backed /dev/shm
+    only when it leaves at least twice that in host memory)."""
+    env = os.environ.get("YLM_BENCH_TMP")
+    if env:
+        return env
+    mem = host_mem_available() or 0
+    try:
+        if shutil.disk_usage("/dev/shm").free > need_bytes * 1.2 and mem > need_bytes * 4:
+            return "/dev/shm"
+    except OSError:
+        pass
+    d = tempfile.gettempdir()
+    if shutil.disk_usage(d).free < need_bytes * 1.2:
+        raise RuntimeError(f"no room for a {need_bytes / 2**30:.1f} GiB snapshot in {d}")
+    return d
+
+
+def snapshot_bytes(spec, esize):
+    return spec.n_params() * esize
+
+
 # ---------------------------------------------------------------- reference runs
 def write_snapshot(tmp, spec, dtype):
     from yalama_b200 import synth
     root = os.path.join(tmp, f"model_{dtype}")
-    synth.write_snapshot(root, spec, seed=WORKLOAD["weight_seed"], dtype=dtype, fast=True)
+    synth.write_snapshot(root, spec, seed=SEEDS["weight_seed"], dtype=dtype, fast=True)
     return root
 
 
-def run_reference_binary(binary, root, prompt_file, n_decode, warmup, threads=None, timeout=1800):
+def run_reference_binary(binary, root, prompt_file, n_decode, warmup, top_k, temp, threads=None, timeout=1800):
     cmd = [binary, "--model", root, "--prompt", prompt_file, "--decode", str(n_decode), "--warmup", str(warmup),
-           "--topk", str(WORKLOAD["top_k"]), "--temp", str(WORKLOAD["temperature"]), "--seed",
-           str(WORKLOAD["sample_seed"])]
+           "--topk", str(top_k), "--temp", str(temp), "--seed", str(SEEDS["sample_seed"])]
     if threads:
         cmd += ["--threads", str(threads)]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
@@ -157,34 +216,46 @@ def run_reference_binary(binary, root, prompt_file, n_decode, warmup, threads=No
     return json.loads(r.stdout.strip().splitlines()[-1])
 
 
-def cpu_reference(spec, n_decode, warmup):
-    """The reference's own forward (LibTorch, CPU, FP32) on this host's cores."""
+def cpu_reference(spec, prompt_len, n_decode, warmup, top_k, temp):
+    """The reference's own forward (LibTorch, CPU, FP32) on this host's cores,
+    on a bounded sample: at most CPU_SAMPLE_PROMPT prompt tokens, then
+    `warmup` untimed and `n_decode` timed decode tokens."""
     from yalama_b200 import synth
     threads = os.cpu_count() or 1
-    with tempfile.TemporaryDirectory(dir=os.environ.get("YLM_BENCH_TMP")) as tmp:
-        pf = os.path.join(tmp, "prompt.bin")
-        synth.write_ids(pf, synth.prompt_ids(WORKLOAD["prompt_seed"], WORKLOAD["prompt"], spec.vocab))
-        if os.path.exists(REF_CPU):
+    p = min(prompt_len, CPU_SAMPLE_PROMPT)
+    need = snapshot_bytes(spec, 4)
+    mem = host_mem_available()
+    if os.path.exists(REF_CPU):
+        # the reference clones every tensor out of the mapped shard: the file's
+        # pages plus a private copy must fit in host memory
+        if mem is not None and mem < need * 2.5:
+            raise RuntimeError(f"host memory {mem / 2**30:.0f} GiB < 2.5 x the {need / 2**30:.0f} GiB FP32 weights")
+        with tempfile.TemporaryDirectory(dir=scratch_dir(need)) as tmp:
+            pf = os.path.join(tmp, "prompt.bin")
+            synth.write_ids(pf, synth.prompt_ids(SEEDS["prompt_seed"], p, spec.vocab))
             root = write_snapshot(tmp, spec, "F32")
-            res = run_reference_binary(REF_CPU, root, pf, n_decode + warmup, warmup, threads)
-            kind = "reference"
-        else:
-            res = cpu_port(spec, n_decode, warmup)
-            kind = "port"
-    return res, kind, threads
+            res = run_reference_binary(REF_CPU, root, pf, n_decode + warmup, warmup, top_k, temp, threads)
+        kind = "reference"
+    else:
+        res = cpu_port(spec, p, n_decode, warmup)
+        kind = "port"
+    sample = (f"{res['timed_tokens']} timed decode tokens ({warmup} untimed) after a {p}-token prefill of the "
+              f"same {spec.hidden}-wide {spec.layers}-layer model, {sampling_desc(top_k, temp)}, FP32; decode is "
+              f"bound by the FP32 weight stream, which the shorter context leaves unchanged")
+    return res, kind, threads, sample
 
 
-def cpu_port(spec, n_decode, warmup):
+def cpu_port(spec, prompt_len, n_decode, warmup):
     """Fallback when the reference binary is absent: the numpy restatement."""
     import numpy as np
     from yalama_b200 import synth
     from oracle.model import OracleModel
-    rng = np.random.default_rng(WORKLOAD["weight_seed"])
+    rng = np.random.default_rng(SEEDS["weight_seed"])
     w = {n: (np.ones(s, np.float32) if n.endswith("norm.weight")
              else rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for n, s in spec.tensor_shapes()}
     m = OracleModel(spec, w, mode="f32")
     m.begin_infer()
-    ids = synth.prompt_ids(WORKLOAD["prompt_seed"], WORKLOAD["prompt"], spec.vocab)
+    ids = synth.prompt_ids(SEEDS["prompt_seed"], prompt_len, spec.vocab)
     t0 = time.perf_counter()
     _, lg = m.infer(ids)
     first = time.perf_counter() - t0
@@ -204,70 +275,77 @@ def bench_reference(a):
         return
     from yalama_b200 import synth
     spec = synth.PRESETS[a.preset]
-    res, kind, threads = cpu_reference(spec, a.steps, a.warmup)
+    try:
+        res, kind, threads, sample = cpu_reference(spec, a.prompt, a.steps, a.warmup, a.top_k, a.temperature)
+    except Exception as ex:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path could not run: {str(ex)[:200]}"}),
+              flush=True)
+        return
     v = res["tokens_per_second"]
-    sample = (f"{res['timed_tokens']} decode tokens after a {WORKLOAD['prompt']}-token prefill "
-              f"({a.warmup} untimed warm-up tokens), top-k 40 / temperature 0.6, FP32")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 / v if v else None,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
-            "config": {"workload": f"{a.preset} batch-1 decode, prompt {WORKLOAD['prompt']}, top-k 40, temp 0.6",
+            "config": {"workload": workload_desc(a, spec),
                        "path": "reference LibTorch CPU path (ModelBase::Infer + ChatSession::Sample)"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+def workload_desc(a, spec):
+    return (f"{a.preset}-shaped FP16{f' ({a.layers} layers)' if a.layers else ''}, batch 1, prompt {a.prompt}, "
+            f"{a.decode} generated tokens, {sampling_desc(a.top_k, a.temperature)}")
+
+
+def gpu_reference(spec, prompt, top_k, temp):
+    """The reference's LibTorch CUDA builds on this GPU: FP16 (the storage type
+    of this engine) and BF16 (the reference as shipped), 128 timed decode
+    tokens after the full prompt, wall clock per token as ChatSession times it."""
+    from yalama_b200 import synth
+    out = {}
+    need = snapshot_bytes(spec, 2)
+    with tempfile.TemporaryDirectory(dir=scratch_dir(need * 2)) as tmp:
+        pf = os.path.join(tmp, "prompt.bin")
+        synth.write_ids(pf, prompt)
+        for key, binary, dtype in (("reference_gpu_fp16", REF_GPU, "F16"), ("reference_gpu_bf16", REF_GPU_BF16, "BF16")):
+            if not os.path.exists(binary):
+                continue
+            try:
+                root = write_snapshot(tmp, spec, dtype)
+                res = run_reference_binary(binary, root, pf, 128 + 4, 4, top_k, temp)
+                shutil.rmtree(root, ignore_errors=True)
+                out[key] = {"value": res["tokens_per_second"], "unit": "tok/s",
+                            "first_token_ms": res["first_token_s"] * 1e3, "load_s": res.get("load_s"),
+                            "sample": f"{res['timed_tokens']} decode tokens (4 untimed) after the {len(prompt)}-token "
+                                      f"prefill, {sampling_desc(top_k, temp)}, LibTorch CUDA "
+                                      f"{dtype} on this GPU (wall clock per token, as ChatSession times it)"}
+            except Exception as ex:
+                out[key] = {"value": None, "error": str(ex)[:300]}
+    return out
+
+
 # ---------------------------------------------------------------- our engine
-def gemv_roofline(spec, hbm_peak, peak_kind):
-    """The dominant kernel (gate-up GEMV, [2I, H]) timed alone with CUDA events on
-    the launching stream; 4 weight copies rotate so every launch streams from HBM."""
-    import numpy as np
-    import torch
-    from yalama_b200 import engine as E
-    n, k = 2 * spec.intermediate, spec.hidden
-    ws = [(torch.randn(n, k, device="cuda", dtype=torch.float16) * 0.02) for _ in range(4)]
-    x = torch.randn(k, device="cuda", dtype=torch.float16)
-    y = torch.empty(n, device="cuda", dtype=torch.float16)
-    s = torch.cuda.current_stream()
-    sp = ctypes.c_void_p(s.cuda_stream)
-    L = E.lib()
-    for i in range(8):
-        E.check(L.ylm_k_gemv(ctypes.c_void_p(ws[i % 4].data_ptr()), n, k, ctypes.c_void_p(x.data_ptr()),
-                             ctypes.c_void_p(y.data_ptr()), sp), "gemv")
-    iters = 64
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    torch.cuda._sleep(1000000)  # keep the stream busy while the launches are queued
-    a.record(s)
-    for i in range(iters):
-        L.ylm_k_gemv(ctypes.c_void_p(ws[i % 4].data_ptr()), n, k, ctypes.c_void_p(x.data_ptr()),
-                     ctypes.c_void_p(y.data_ptr()), sp)
-    b.record(s)
-    b.synchronize()
-    ms = a.elapsed_time(b) / iters
-    alg = n * k * 2 + k * 2 + n * 2
-    achieved = alg / (ms * 1e-3) / 1e9
-    del ws
-    return {"kernel": f"gemv_kernel (gate-up shape {n}x{k}, FP16)", "bound": "hbm", "achieved": achieved,
-            "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-            "traffic": profile_traffic("gemv_gateup_llama3.2-3b.txt"), "algorithmic_bytes": alg,
-            "avg_launch_us": ms * 1e3}
-
-
 def segment_roofline(eng, spec, hbm_peak, peak_kind):
     """The dominant kernel of the persistent path: one decode GEMV segment (a
-    middle layer's O, gate-up, down and the next layer's QKV, one cooperative
-    launch) timed alone with CUDA events on the engine stream, back to back;
-    its weights (201 MB for the 3B shape) exceed L2, so every launch streams
-    them from HBM. Algorithmic bytes = the segment's weights."""
+    middle layer's O, gate-up, down and the next layer's QKV) timed alone with
+    CUDA events on the engine stream, back to back; its weights (436 MB for
+    the 8B shape) exceed L2, so every launch streams them from HBM.
+    Algorithmic bytes = the segment's weights."""
     ms, wbytes = eng.time_segment(spec.layers // 2, 48)
     achieved = wbytes / (ms * 1e-3) / 1e9
     return {"kernel": "decode_segment_kernel (O + gate-up + down + next QKV of one layer, FP16)",
             "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-            "peak_kind": peak_kind, "traffic": profile_traffic("decode_segment_llama3.2-3b.txt"),
+            "peak_kind": peak_kind, "traffic": profile_traffic(f"decode_segment_{spec_name(spec)}.txt"),
             "algorithmic_bytes": wbytes, "avg_launch_us": ms * 1e3}
+
+
+def spec_name(spec):
+    from yalama_b200 import synth
+    for k, v in synth.PRESETS.items():
+        if v.hidden == spec.hidden and v.vocab == spec.vocab and v.model_type == spec.model_type:
+            return k
+    return "custom"
 
 
 def decode_bytes_per_token(spec, ctx, tp):
@@ -283,10 +361,82 @@ def decode_bytes_per_token(spec, ctx, tp):
     return (w + kv) / tp
 
 
-def bench_ours(a):
-    import numpy as np
+def run_workload(a, rank, world, local, pg, nccl_id, spec, steps, warmup, e2e_requests, with_roofline):
+    """Time `steps` requests of the workload (after `warmup`); returns a dict of
+    the measured numbers, identical on every rank (max over ranks)."""
     import torch
     from yalama_b200 import engine as E
+    from yalama_b200 import synth
+
+    cfg = E.config_from_spec(spec)
+    eng = E.Engine(None, cfg, nccl_id=nccl_id, device=local, tp_rank=rank, tp_size=world,
+                   init_seed=SEEDS["weight_seed"], decode_persistent=int(a.decode_path == "persistent"))
+    greedy = a.top_k == 0
+    eng.set_sampling(greedy=greedy, top_k=a.top_k or 40, temperature=a.temperature, seed=SEEDS["sample_seed"])
+    prompt = synth.prompt_ids(SEEDS["prompt_seed"], a.prompt, spec.vocab)
+    n_dec = a.decode - 1
+
+    def request():
+        eng.begin_infer()
+        st, _ = eng.infer(prompt)
+        assert st == E.Status.OK, st
+        pf = eng.last_prefill_ms()
+        eng.sample(True)
+        ms = eng.time_decode(n_dec)
+        return pf, ms * n_dec
+
+    def barrier():
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(warmup):
+        request()
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    t_wall = time.perf_counter()
+    pf_ms, dec_ms = 0.0, 0.0
+    eng.reset_exchange_stats()
+    for _ in range(steps):
+        p, d = request()
+        pf_ms += p
+        dec_ms += d
+    barrier()
+    wall = time.perf_counter() - t_wall
+    clk = clocks.stop()
+    xstats = eng.exchange_stats()
+    tm = torch.tensor([pf_ms, dec_ms, xstats["wait_ms"], xstats["tokens"]], dtype=torch.float64)
+    if pg:
+        pg.all_reduce(tm, op=pg.ReduceOp.MAX)
+    pf_ms, dec_ms = float(tm[0]), float(tm[1])
+    r = {"value": steps * n_dec / (dec_ms / 1e3), "prefill_tok_s": steps * a.prompt / (pf_ms / 1e3),
+         "ms_per_step": (pf_ms + dec_ms) / steps, "ms_per_token": dec_ms / (steps * n_dec), "wall": wall,
+         "clocks": clk, "persistent": eng.decode_persistent()}
+    if world > 1:
+        r["exchange_wait_ms_per_token"] = float(tm[2]) / max(1.0, float(tm[3]))
+
+    e2e_tps = []
+    for _ in range(e2e_requests):
+        barrier()
+        g = eng.generate(prompt, a.decode, eos_ids=[])
+        n = len(g["ids"])
+        t = torch.tensor([g["decode_ms"]], dtype=torch.float64)
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_tps.append((n - 1) / (float(t[0]) / 1e3))
+    r["e2e"] = statistics.median(e2e_tps) if e2e_tps else None
+    if world > 1:
+        r["allreduce_nccl_ms_per_token"] = eng.time_allreduce(32)
+    if with_roofline and r["persistent"] and world == 1:
+        r["roofline"] = segment_roofline(eng, spec, *peaks())
+    eng.close()
+    del eng
+    return r
+
+
+def bench_ours(a):
+    import torch
     from yalama_b200 import tp as TP
     from yalama_b200 import synth
 
@@ -306,131 +456,82 @@ def bench_ours(a):
     if a.layers:
         import dataclasses
         spec = dataclasses.replace(spec, layers=a.layers)
-    cfg = E.config_from_spec(spec)
-    eng = E.Engine(None, cfg, nccl_id=nccl_id, device=local, tp_rank=rank, tp_size=world,
-                   init_seed=WORKLOAD["weight_seed"], decode_persistent=int(a.decode_path == "persistent"))
-    eng.set_sampling(greedy=False, top_k=WORKLOAD["top_k"], temperature=WORKLOAD["temperature"],
-                     seed=WORKLOAD["sample_seed"])
-    prompt = synth.prompt_ids(WORKLOAD["prompt_seed"], a.prompt, spec.vocab)
-    n_dec = a.decode - 1
 
-    def request():
-        eng.begin_infer()
-        st, _ = eng.infer(prompt)
-        assert st == E.Status.OK, st
-        pf = eng.last_prefill_ms()
-        eng.sample(True)
-        ms = eng.time_decode(n_dec)
-        return pf, ms * n_dec
-
-    def barrier():
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(a.warmup):
-        request()
-    barrier()
-    clocks = Clocks(local)
-    clocks.start()
-    t_wall = time.perf_counter()
-    pf_ms, dec_ms = 0.0, 0.0
-    for _ in range(a.steps):
-        p, d = request()
-        pf_ms += p
-        dec_ms += d
-    barrier()
-    wall = time.perf_counter() - t_wall
-    clk = clocks.stop()
-    tm = torch.tensor([pf_ms, dec_ms], dtype=torch.float64)
-    if pg:
-        pg.all_reduce(tm, op=pg.ReduceOp.MAX)
-    pf_ms, dec_ms = float(tm[0]), float(tm[1])
-    value = a.steps * n_dec / (dec_ms / 1e3)
-    prefill_tps = a.steps * a.prompt / (pf_ms / 1e3)
-
-    # e2e: the C-ABI token loop with host buffers
-    e2e_tps = []
-    for _ in range(a.e2e_requests):
-        barrier()
-        r = eng.generate(prompt, a.decode, eos_ids=[])
-        n = len(r["ids"])
-        t = torch.tensor([r["decode_ms"]], dtype=torch.float64)
-        if pg:
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        e2e_tps.append((n - 1) / (float(t[0]) / 1e3))
-    e2e_v = statistics.median(e2e_tps) if e2e_tps else None
-    # bytes crossing the host boundary per request: prompt in, 64-byte step state in/out per call
-    calls = 2 + (a.decode - 1)
-    h2d = a.prompt * 8 + 64 * calls
-    d2h = 64 * calls
-
+    r = run_workload(a, rank, world, local, pg, nccl_id, spec, a.steps, a.warmup, a.e2e_requests,
+                     not a.no_roofline)
     hbm, peak_kind = peaks()
     ctx = a.prompt + a.decode // 2
     bpt = decode_bytes_per_token(spec, ctx, world)
-    ms_tok = dec_ms / (a.steps * n_dec)
-    persistent = eng.decode_persistent()
-    seg_roof = None
-    if persistent and world == 1 and not a.no_roofline:
-        seg_roof = segment_roofline(eng, spec, *peaks())
-    step_roof = {"bytes_per_token_per_gpu": bpt, "ms_per_token": ms_tok,
+    ms_tok = r["ms_per_token"]
+    step_roof = {"bytes_per_token_per_gpu": bpt, "mean_context": ctx, "ms_per_token": ms_tok,
                  "achieved_gbs": bpt / (ms_tok * 1e-3) / 1e9, "peak_gbs": hbm,
                  "frac": bpt / (ms_tok * 1e-3) / 1e9 / hbm, "frac_of_8000": bpt / (ms_tok * 1e-3) / 1e9 / 8000.0,
                  "peak_kind": peak_kind}
-    eng.close()
-    del eng
+
+    extra = None
+    if world == 1 and not a.no_extra and not a.layers and a.workload != EXTRA_WORKLOAD:
+        b = argparse.Namespace(**vars(a))
+        b.preset, b.prompt, b.decode, b.top_k, b.temperature = WORKLOADS[EXTRA_WORKLOAD]
+        espec = synth.PRESETS[b.preset]
+        er = run_workload(b, rank, world, local, pg, nccl_id, espec, 2, 1, 1, False)
+        ebpt = decode_bytes_per_token(espec, b.prompt + b.decode // 2, 1)
+        extra = {"workload": workload_desc(b, espec), "value": er["value"], "unit": "tok/s",
+                 "ms_per_token": er["ms_per_token"], "prefill_tok_s": er["prefill_tok_s"],
+                 "decode_roofline_frac": ebpt / (er["ms_per_token"] * 1e-3) / 1e9 / hbm,
+                 "e2e": er["e2e"], "steps": 2, "warmup": 1}
 
     if rank != 0:
         if pg:
             pg.barrier()
         return
-    roof = seg_roof
-    if roof is None and world == 1 and not a.no_roofline:
-        roof = gemv_roofline(spec, hbm, peak_kind)
     # decode launches per token: persistent path = one GEMV segment per layer
     # plus one, attention per layer, sampler; per-op graph = QKV, attention,
     # O, gate-up, down per layer (+ residual adds with tensor parallelism),
     # lm_head, sampler; NCCL's all-reduce / all-gather kernels are not counted
-    if persistent:
+    if r["persistent"]:
         launches_per_token = 2 * spec.layers + 2
     else:
         launches_per_token = spec.layers * (5 if world == 1 else 7) + 2
+    n_dec = a.decode - 1
     prefill_launches = 1 + spec.layers * 8 + 1
     gpu_launches = a.steps * (prefill_launches + 1 + n_dec * launches_per_token)
-    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": (pf_ms + dec_ms) / a.steps, "higher_is_better": True,
+    calls = 2 + (a.decode - 1)
+    h2d = a.prompt * 8 + 64 * calls
+    d2h = 64 * calls
+    line = {"metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init N(0,0.02) weights, uniform-random prompt ids)",
-            "config": {"workload": f"{a.preset}-shaped FP16{f' ({a.layers} layers)' if a.layers else ''}, batch 1, prompt {a.prompt}, {a.decode} generated tokens, "
-                                   f"top-k {WORKLOAD['top_k']}, temperature {WORKLOAD['temperature']}",
-                       "parallelism": f"tp{world}", "decode_path": "persistent GEMV segments" if persistent else "per-op graph",
-                       "l2": "weights 6.4 GB >> 126 MB L2 (no flush needed)",
+            "config": {"workload": workload_desc(a, spec), "parallelism": f"tp{world}",
+                       "decode_path": "persistent GEMV segments" if r["persistent"] else "per-op graph",
+                       "l2": f"weights {bpt * world / 1e9:.1f} GB >> 126 MB L2 (no flush needed)",
                        "timing": "CUDA events on the engine stream; value = decode tokens / decode time"},
-            "prefill_tok_s": prefill_tps, "decode_roofline": step_roof, "roofline": roof,
-            "e2e": {"value": e2e_v, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "prefill_tok_s": r["prefill_tok_s"], "decode_roofline": step_roof, "roofline": r.get("roofline"),
+            "e2e": {"value": r["e2e"], "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "ylm_generate (C ABI), host prompt in, host ids out, per-token sync"},
-            "gpu_launches": gpu_launches, "wall_s_timed": wall, "clocks": clk}
+            "gpu_launches": gpu_launches, "wall_s_timed": r["wall"], "clocks": r["clocks"]}
+    if world > 1:
+        line["allreduce"] = {
+            "exchange_wait_ms_per_token": r["exchange_wait_ms_per_token"],
+            "nccl_ms_per_token": r["allreduce_nccl_ms_per_token"],
+            "count_per_token": 2 * spec.layers, "bytes_each": spec.hidden * 2,
+            "note": "exchange_wait: device time (%globaltimer) from a segment's first partial store to the "
+                    "arrival of every peer's partials, summed over the step's exchanges (block 0); nccl: "
+                    "2L back-to-back NCCL all-reduces of [hidden] FP16 in a CUDA graph on the same ranks"}
+    if extra:
+        line["extra_" + EXTRA_WORKLOAD.replace(".", "_").replace("-", "_")] = extra
     if world == 1 and not a.no_cpu_baseline:
         try:
-            res, kind, threads = cpu_reference(spec, 4, 1)
+            res, kind, threads, sample = cpu_reference(spec, a.prompt, 4, 1, a.top_k, a.temperature)
             line["cpu_baseline"] = {"value": res["tokens_per_second"], "unit": "tok/s", "cores": threads,
-                                    "kind": kind,
-                                    "sample": f"{res['timed_tokens']} decode tokens after a {a.prompt}-token "
-                                              f"prefill (1 warm-up token), FP32, same model shape"}
+                                    "kind": kind, "sample": sample}
         except Exception as ex:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(ex)[:300]}
-    if world == 1 and not a.no_ref_gpu and os.path.exists(REF_GPU):
+    if world == 1 and not a.no_ref_gpu and not a.layers:
+        from yalama_b200 import synth as sy
         try:
-            from yalama_b200 import synth as sy
-            with tempfile.TemporaryDirectory(dir=os.environ.get("YLM_BENCH_TMP")) as tmp:
-                pf = os.path.join(tmp, "prompt.bin")
-                sy.write_ids(pf, prompt)
-                root = write_snapshot(tmp, spec, "F16")
-                res = run_reference_binary(REF_GPU, root, pf, 32 + 3, 3)
-            line["reference_gpu_fp16"] = {"value": res["tokens_per_second"], "unit": "tok/s",
-                                          "first_token_ms": res["first_token_s"] * 1e3,
-                                          "sample": "32 decode tokens after the 512-token prefill, top-k 40, "
-                                                    "LibTorch CUDA FP16 on this GPU (wall clock per token)"}
+            line.update(gpu_reference(spec, sy.prompt_ids(SEEDS["prompt_seed"], a.prompt, spec.vocab), a.top_k,
+                                      a.temperature))
         except Exception as ex:
             line["reference_gpu_fp16"] = {"value": None, "error": str(ex)[:300]}
     print(json.dumps(line), flush=True)

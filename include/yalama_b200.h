@@ -179,6 +179,28 @@ int ylm_decode_path(ylm_engine *e, int32_t *persistent);
  * No counterpart in the reference (benchmark support). */
 int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per_launch, double *weight_bytes);
 
+/* Tensor-parallel exchange timing of the persistent path: *wait_ms = the
+ * device time (%globaltimer) that block 0 spent in the all-reduce exchanges
+ * fused into the O and down epilogues, from its first partial store until
+ * every rank's partial of its row had arrived, summed since the last reset;
+ * *exchanges = their number; *steps = decode steps since the last reset.
+ * reset != 0 clears the three afterwards. Zeros without tensor parallelism.
+ * No counterpart in the reference (it runs on one GPU). */
+int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *exchanges, double *steps);
+/* Time one decode step's collectives alone: 2 x num_layers NCCL all-reduces
+ * of [hidden] FP16 back to back in a CUDA graph on the engine's communicator,
+ * averaged over `iters` replays. Every rank must call it together.
+ * YLM_UNSUPPORTED without tensor parallelism. Benchmark support; no
+ * counterpart in the reference. */
+int ylm_time_allreduce(ylm_engine *e, int32_t iters, double *ms_per_step);
+
+/* Decode-attention kernel for all later launches in this process (and CUDA
+ * graphs captured afterwards): 0 (default) one thread-block cluster per KV
+ * head where the device can launch clusters, else the split-K kernel; 1 the
+ * split-K kernel (global partials and per-KV-head tickets) everywhere. For
+ * tests and diagnostics; no counterpart in the reference. */
+int ylm_set_attention_path(int32_t split_kernel);
+
 /* ---- kernel-level entry points (device pointers; stream = cudaStream_t or NULL) */
 /* y[n] = W[n,k] x[k], FP16 in and out, FP32 accumulation (the decode GEMV). */
 int ylm_k_gemv(const void *w, int32_t n, int32_t k, const void *x, void *y, void *stream);
@@ -204,10 +226,13 @@ int ylm_k_decode_attention(const void *qkv, const void *q_norm, const void *k_no
  * cannot allocate device memory (their memory is owned by their own pool, or an
  * allocation's synchronisation is not acceptable where they call from). It has
  * no counterpart in the reference. Scratch lives in one 2 MiB array that the
- * library reserves on every GPU that loads it, for the life of the process:
- * sizes needing more (hq x splits x 130 floats + KV-head tickets) return
- * YLM_UNSUPPORTED. Calls share that array: calls that overlap on the GPU race,
- * so serialise them. The first call on a device looks the array up (with that
+ * library reserves on every GPU that loads it, for the life of the process.
+ * The cluster kernel needs only a 256-byte step state there; the split-K
+ * kernel (no cluster launch, or ylm_set_attention_path(1)) also keeps its
+ * partials (hq x splits x 130 floats) and KV-head tickets there, and shapes
+ * whose partials do not fit return YLM_UNSUPPORTED (only past ~4000 query
+ * heads). Calls share that array: calls that overlap on the GPU race, so
+ * serialise them. The first call on a device looks the array up (with that
  * device current) and should come before any stream capture. */
 int ylm_k_decode_attention_noalloc(const void *qkv, const void *q_norm, const void *k_norm, float eps,
                                    const void *rope_cos, const void *rope_sin, int32_t max_pos, void *k_cache,

@@ -18,7 +18,12 @@
 //   ref_harness --model <hf_repo_root> --prompt <ids.bin int64> --decode <n>
 //               [--out <file>] [--kvgb <n>] [--nokv] [--topk K --temp T --seed S]
 //               [--mask <ids.bin int64>] [--threads N] [--warmup W]
+//   ref_harness --sample-fixture <in.bin> <out.bin> --topk K --temp T [--mask <ids.bin int64>]
 // --warmup W leaves the first W decode tokens out of the timed sum.
+// --sample-fixture runs only ChatSession::Sample's LibTorch ops (without the
+// draw) on given FP16 logit rows on the CUDA device: in.bin = int64 rows,
+// int64 V, rows x V FP16 bit patterns; out.bin per row = int64 argmax id,
+// K x int64 top-k ids, K x FP16 top-k values, K x FP16 softmax probabilities.
 #include "Model.h"
 #include "ConfigManager.h"
 #include <torch/torch.h>
@@ -26,6 +31,7 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <limits>
 #include <iostream>
 #include <string>
 #include <vector>
@@ -68,6 +74,51 @@ int64_t sample_like_reference(torch::Tensor &last, bool greedy, int topk, float 
     }
     return next.to(torch::kCPU, false, true).item<int64_t>();
 }
+// The greedy pick and the top-k candidates of ChatSession::Sample
+// (src/ChatSession.cpp:560-593) on FP16 rows, with the same ops in the same
+// order, everything before torch::multinomial.
+int sample_fixture(const std::string &in_path, const std::string &out_path, int topk, float temp,
+                   const std::vector<int64_t> &masked)
+{
+    std::ifstream f(in_path, std::ios::binary);
+    if (!f)
+        throw std::runtime_error("cannot open " + in_path);
+    int64_t rows = 0, V = 0;
+    f.read(reinterpret_cast<char *>(&rows), 8);
+    f.read(reinterpret_cast<char *>(&V), 8);
+    std::vector<uint16_t> buf((size_t)V);
+    FILE *out = std::fopen(out_path.c_str(), "wb");
+    if (!out)
+        throw std::runtime_error("cannot write " + out_path);
+    for (int64_t r = 0; r < rows; r++)
+    {
+        f.read(reinterpret_cast<char *>(buf.data()), V * 2);
+        torch::Tensor last = torch::from_blob(buf.data(), {1, V}, torch::kInt16)
+                                 .clone()
+                                 .view(torch::kHalf)
+                                 .to(torch::Device(torch::kCUDA));
+        int64_t greedy = last.argmax(-1).to(torch::kCPU).item<int64_t>();
+        torch::Tensor scaled = last / temp;
+        // ChatSession writes -1e9f (ChatSession.cpp:573-576), which BF16 holds;
+        // LibTorch refuses to convert it to FP16 ("cannot be converted to type
+        // c10::Half without overflow"), so on FP16 logits the masked ids get
+        // -inf, the value -1e9 takes in any FP16 rounding
+        for (auto id : masked)
+            scaled[0][id] = -std::numeric_limits<float>::infinity();
+        auto tk = torch::topk(scaled, topk, -1);
+        torch::Tensor probs = torch::softmax(std::get<0>(tk), -1);
+        torch::Tensor ids = std::get<1>(tk).to(torch::kCPU).contiguous();
+        torch::Tensor vals = std::get<0>(tk).to(torch::kCPU).contiguous().view(torch::kInt16);
+        torch::Tensor pr = probs.to(torch::kCPU).contiguous().view(torch::kInt16);
+        std::fwrite(&greedy, 8, 1, out);
+        std::fwrite(ids.data_ptr<int64_t>(), 8, topk, out);
+        std::fwrite(vals.data_ptr<int16_t>(), 2, topk, out);
+        std::fwrite(pr.data_ptr<int16_t>(), 2, topk, out);
+    }
+    std::fclose(out);
+    std::printf("{\"rows\": %lld, \"vocab\": %lld, \"topk\": %d}\n", (long long)rows, (long long)V, topk);
+    return 0;
+}
 } // namespace
 
 int main(int argc, char **argv)
@@ -77,6 +128,7 @@ int main(int argc, char **argv)
     float temp = 0.6f;
     int64_t seed = 0;
     bool kv = true;
+    std::string fixture_in, fixture_out;
 
     for (int i = 1; i < argc; i++)
     {
@@ -98,11 +150,19 @@ int main(int argc, char **argv)
         else if (a == "--mask") mask_path = next();
         else if (a == "--threads") threads = std::stoi(next());
         else if (a == "--warmup") warmup = std::stoi(next());
+        else if (a == "--sample-fixture")
+        {
+            fixture_in = next();
+            fixture_out = next();
+        }
         else throw std::runtime_error("unknown argument " + a);
     }
     if (threads > 0)
         torch::set_num_threads(threads);
     torch::manual_seed(seed);
+    if (!fixture_in.empty())
+        return sample_fixture(fixture_in, fixture_out, topk, temp,
+                              mask_path.empty() ? std::vector<int64_t>() : read_ids(mask_path));
 
     // CLI-level settings, as src/main.cpp:20-402 would set them; ConfigManager::Load
     // then fills the rest from the HF snapshot (refs/main -> snapshots/<hash>).

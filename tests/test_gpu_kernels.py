@@ -127,9 +127,20 @@ def ref_prep(x, w_norm, eps, cos, sin):
     return round_f16(round_f16(x * c) + round_f16(rot * s))
 
 
+@pytest.mark.parametrize("split", [0, 1], ids=["cluster", "split_k"])
 @pytest.mark.parametrize("hq,hkv,slot,norm", [(16, 8, 40, True), (24, 8, 767, False), (28, 4, 8300, False),
-                                              (8, 8, 0, False), (64, 8, 100, False), (4, 2, 5, True)])
-def test_decode_attention_step(hq, hkv, slot, norm):
+                                              (8, 8, 0, False), (64, 8, 100, False), (4, 2, 5, True),
+                                              (32, 8, 2560, False)])
+def test_decode_attention_step(hq, hkv, slot, norm, split):
+    # split = 1: the split-K kernel, which runs where cluster launches are unavailable
+    E.check(E.lib().ylm_set_attention_path(split), "path")
+    try:
+        _decode_attention_step(hq, hkv, slot, norm)
+    finally:
+        E.lib().ylm_set_attention_path(0)
+
+
+def _decode_attention_step(hq, hkv, slot, norm):
     rng = np.random.default_rng(hq * 1000 + slot)
     D, cap, max_pos = 128, slot + 64, slot + 16
     pos = max(0, slot - 1)

@@ -77,6 +77,20 @@ def test_family_logits_match_oracle(fam, persistent):
     assert worst < LOGIT_TOL
 
 
+@pytest.mark.parametrize("fam", ["llama", "qwen3"])
+def test_split_attention_kernel_logits_match_oracle(fam):
+    # the split-K decode attention (global partials, last-CTA combine), the
+    # path where cluster launches are unavailable, in both decode paths
+    with E.split_attention():
+        for persistent in (0, 1):
+            spec, eng = make(FAMILIES[fam], decode_persistent=persistent)
+            orc = OracleModel(spec, synth.model_weights(spec, 0), mode="f16", kv_gb=2)
+            prompt = synth.prompt_ids(9, 700, spec.vocab)
+            worst, _ = run_teacher_forced(eng, orc, prompt, 6)
+            eng.close()
+            assert worst < LOGIT_TOL, (persistent, worst)
+
+
 def test_snapshot_load_equals_random_init(tmp_path):
     kw = FAMILIES["qwen2"]
     spec, a = make(kw)
@@ -302,3 +316,27 @@ def test_generate_matches_oracle_greedy(persistent):
             assert top2_gap(lo) < TIE_GAP
             break
         ids = [int(t)]
+
+
+def test_llama3_scaled_rope_matches_oracle():
+    # rope_scaling = 1: the engine's llama3-scaled table (the reference parses
+    # the fields but applies plain theta, so this is checked against the
+    # oracle's scaled table, itself pinned to transformers in test_rope_scaling)
+    scaling = {"rope_type": "llama3", "factor": 32.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+               "original_max_position_embeddings": 8192}
+    kw = dict(FAMILIES["llama"], rope_scaling=scaling)
+    # weights N(0, 0.06): with N(0, 0.02) the attention of this small model is
+    # nearly uniform and the two tables give logits only ~3e-3 apart
+    spec, eng = make(kw, rope_scaling=1, init_std=0.06)
+    w = synth.model_weights(spec, 0, std=0.06)
+    orc = OracleModel(spec, w, mode="f16", rope_scaling=True)
+    plain = OracleModel(spec, w, mode="f16", rope_scaling=False)
+    prompt = synth.prompt_ids(8, 300, spec.vocab)
+    worst, _ = run_teacher_forced(eng, orc, prompt, 8)
+    assert worst < LOGIT_TOL
+    # the scaled and plain tables give clearly different logits at these positions
+    eng.begin_infer()
+    plain.begin_infer()
+    eng.infer(prompt)
+    _, lp = plain.infer(prompt)
+    assert np.max(np.abs(eng.logits() - lp)) > 10 * LOGIT_TOL

@@ -1,0 +1,137 @@
+"""Engine parity against the reference itself at the benchmark shapes.
+
+The reference's own model code (src/models/Model.cpp, ModelBase.cpp, the family
+files and ConfigManager.cpp), compiled unmodified for LibTorch CUDA with FP16
+storage (``oracle/_ref/ref_gpu_f16``, built by ``oracle/ref/Makefile``), runs
+the token loop of ChatSession::Generate (src/ChatSession.cpp:113-230) greedily
+on a snapshot written to disk; the engine loads the same snapshot through its
+own safetensors loader and is teacher-forced with the reference's ids:
+
+- logits within max-abs 2e-2 of the reference's FP16 path at the prefill and
+  at every decode step;
+- the engine's greedy id equals the reference's except at steps where the
+  reference's top-2 logit gap is below 1e-2;
+- ylm_generate's free-running greedy ids equal the reference's up to the first
+  such near-tie.
+
+Shapes: Qwen3-0.6B at full depth (32-token prompt, 128 tokens, as benchmarked)
+and the Llama-3.2-3B, Qwen2.5-7B, Llama-3.1-8B, Mistral-7B-v0.3 and
+Llama-3.1-70B widths with the layer count cut (hidden, heads, intermediate and
+vocabulary as benchmarked; prompt lengths as benchmarked except 70B), so the
+persistent decode segments, the cluster attention and the prefill GEMMs run at
+their real task splits. Both sides use plain RoPE theta (the reference ignores
+rope_scaling, src/models/ModelBase.cpp:372-394) and the reference's decode RoPE
+position (slot - 1, ModelBase.cpp:577-581).
+"""
+import dataclasses
+import os
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+
+from yalama_b200 import engine as E
+from yalama_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_GPU_F16 = os.path.join(ROOT, "oracle", "_ref", "ref_gpu_f16")
+# north_star: logits within max-abs 2e-2 (FP16) of the reference's FP16 path
+LOGIT_TOL = 2e-2
+# greedy ids may differ only where the reference's top-2 logit gap is below this
+TIE_GAP = 1e-2
+
+# name -> (preset, layers (0 = all), prompt tokens, decode steps)
+CASES = {
+    "qwen3-0.6b": ("qwen3-0.6b", 0, 32, 128),
+    "llama3.2-3b-l3": ("llama3.2-3b", 3, 512, 32),
+    "qwen2.5-7b-l2": ("qwen2.5-7b", 2, 8192, 16),
+    "llama3.1-8b-l4": ("llama3.1-8b", 4, 2048, 32),
+    "mistral-7b-l2": ("mistral-7b-v0.3", 2, 2048, 16),
+    "llama3.1-70b-l1": ("llama3.1-70b", 1, 512, 8),
+}
+
+
+def read_ref_out(path):
+    """ref_harness --out: per step int64 V, float32[V] last-row logits, int64 id."""
+    raw = open(path, "rb").read()
+    rows, ids, off = [], [], 0
+    while off < len(raw):
+        v = int(np.frombuffer(raw, np.int64, 1, off)[0])
+        off += 8
+        rows.append(np.frombuffer(raw, np.float32, v, off).copy())
+        off += 4 * v
+        ids.append(int(np.frombuffer(raw, np.int64, 1, off)[0]))
+        off += 8
+    return np.stack(rows), ids
+
+
+def top2_gap(lg):
+    s = np.partition(lg.astype(np.float64), -2)[-2:]
+    return float(s[1] - s[0])
+
+
+def run_reference(root, prompt, steps, tmp):
+    pf = os.path.join(tmp, "prompt.bin")
+    synth.write_ids(pf, prompt)
+    out = os.path.join(tmp, "ref_out.bin")
+    r = subprocess.run([REF_GPU_F16, "--model", root, "--prompt", pf, "--decode", str(steps), "--out", out],
+                       capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return read_ref_out(out)
+
+
+@pytest.fixture(scope="module")
+def ref_binary():
+    if not os.path.exists(REF_GPU_F16):
+        pytest.fail(f"{REF_GPU_F16} is missing: build it with `make -C oracle/ref` where the reference sources are")
+    return REF_GPU_F16
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_engine_matches_reference_fp16(case, ref_binary, tmp_path):
+    preset, layers, n_prompt, steps = CASES[case]
+    spec = synth.PRESETS[preset]
+    if layers:
+        spec = dataclasses.replace(spec, layers=layers)
+    root = str(tmp_path / "model")
+    snap = synth.write_snapshot(root, spec, seed=0, dtype="F16", fast=True)
+    prompt = synth.prompt_ids(11, n_prompt, spec.vocab)
+    try:
+        ref_rows, ref_ids = run_reference(root, prompt, steps, str(tmp_path))
+        assert len(ref_ids) == steps + 1, len(ref_ids)
+        eng = E.Engine(snap, E.config_from_spec(spec))
+        try:
+            assert eng.decode_persistent()
+            # teacher-forced: prefill, then every reference id
+            eng.begin_infer()
+            ids = list(prompt)
+            worst, worst_step, near_ties = 0.0, -1, 0
+            for step in range(steps + 1):
+                st, _ = eng.infer(ids)
+                assert st == E.Status.OK, (step, st)
+                lg = eng.logits()
+                d = float(np.max(np.abs(lg - ref_rows[step])))
+                if d > worst:
+                    worst, worst_step = d, step
+                if int(np.argmax(lg)) != ref_ids[step]:
+                    gap = top2_gap(ref_rows[step])
+                    assert gap < TIE_GAP, (step, int(np.argmax(lg)), ref_ids[step], gap)
+                    near_ties += 1
+                ids = [ref_ids[step]]
+            print(f"{case}: max |logit diff| vs reference FP16 = {worst:.3e} (step {worst_step}), "
+                  f"{near_ties} near-tie id differences in {steps + 1} steps")
+            assert worst < LOGIT_TOL, (worst, worst_step)
+            # free running through the C ABI's token loop
+            g = eng.generate(prompt, steps + 1, eos_ids=[])
+            assert g["status"] == E.Status.OK
+            for step, t in enumerate(g["ids"]):
+                if int(t) != ref_ids[step]:
+                    assert top2_gap(ref_rows[step]) < TIE_GAP, (step, int(t), ref_ids[step])
+                    break
+        finally:
+            eng.close()
+    finally:
+        shutil.rmtree(root, ignore_errors=True)

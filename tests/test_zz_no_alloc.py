@@ -33,8 +33,7 @@ def _tables(max_pos, theta=1e6):
             torch.from_numpy(np.sin(ang.astype(np.float64)).astype(np.float16)).cuda())
 
 
-@pytest.mark.parametrize("hq,hkv,slot,norm", [(24, 8, 767, False), (16, 8, 40, True), (28, 4, 5000, False)])
-def test_noalloc_matches_allocating_entry_point(hq, hkv, slot, norm):
+def _run_pair(hq, hkv, slot, norm):
     L = E.lib()
     D, cap, max_pos = 128, slot + 32, slot + 8
     g = torch.Generator().manual_seed(hq * 131 + slot)
@@ -63,9 +62,35 @@ def test_noalloc_matches_allocating_entry_point(hq, hkv, slot, norm):
         assert torch.equal(kc_a, kc_b) and torch.equal(vc_a, vc_b), call
 
 
-def test_noalloc_rejects_sizes_beyond_its_scratch():
-    # one KV head and 8 query heads per group at many splits still fits; an
-    # impossible head count is refused before touching the device
+CASES = [(24, 8, 767, False), (16, 8, 40, True), (28, 4, 5000, False)]
+
+
+@pytest.mark.parametrize("hq,hkv,slot,norm", CASES)
+def test_noalloc_matches_allocating_entry_point(hq, hkv, slot, norm):
+    # the cluster kernel: the fixed array holds only the step state
+    _run_pair(hq, hkv, slot, norm)
+
+
+@pytest.mark.parametrize("hq,hkv,slot,norm", CASES)
+def test_noalloc_matches_allocating_entry_point_split_kernel(hq, hkv, slot, norm):
+    # the split-K kernel: the fixed array also holds the partials and the
+    # KV-head tickets, which the previous call left behind
+    with E.split_attention():
+        _run_pair(hq, hkv, slot, norm)
+
+
+def test_noalloc_rejects_null_buffers():
     L = E.lib()
     assert L.ylm_k_decode_attention_noalloc(None, None, None, 1e-6, None, None, 16, None, None, 8, 4, 2, 0, 0, None,
                                             None) == E.Status.INVALID_ARG
+
+
+def test_noalloc_rejects_partials_beyond_its_scratch():
+    # split-K partials of 4096 query heads over 512 KV heads (one split each):
+    # 4096 x 130 floats > 2 MiB. The size check returns before any device
+    # access, so the non-null placeholder pointers are never dereferenced.
+    L = E.lib()
+    p = ctypes.c_void_p(256)
+    with E.split_attention():
+        st = L.ylm_k_decode_attention_noalloc(p, None, None, 1e-6, p, p, 16, p, p, 8, 4096, 512, 0, 0, p, None)
+    assert st == E.Status.UNSUPPORTED

@@ -353,6 +353,7 @@ constexpr int ATC_MAX_SPLITS = 16; // largest cluster
 constexpr int ATC_MIN_SPLITS = 8;  // smallest cluster (the portable size)
 
 static int g_cluster_splits = 0; // 16, 8, or 0 (no cluster launch: split-K kernel)
+static int g_force_split = 0;    // 1: the split-K kernel even where clusters launch (tests, diagnostics)
 
 template <int G>
 __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArgs a)
@@ -693,11 +694,15 @@ cudaError_t attn_prepare()
     return e;
 }
 
+void attn_force_split_kernel(bool on) { g_force_split = on ? 1 : 0; }
+
+bool attn_uses_split_kernel() { return g_force_split || g_cluster_splits == 0; }
+
 cudaError_t attn_decode_launch(const AttnArgs &a, cudaStream_t s, bool pdl)
 {
     if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.splits <= 0)
         return cudaErrorInvalidValue;
-    const int S = g_cluster_splits;
+    const int S = g_force_split ? 0 : g_cluster_splits;
     if (S > 0)
         switch (a.hq / a.hkv)
         {

@@ -11,9 +11,14 @@
 // it, for the life of the process.
 //
 // Limits and rules (also stated in include/yalama_b200.h):
-//   - scratch is YLM_NOALLOC_SCRATCH_BYTES (2 MiB): step state + hq x splits x
-//     130 floats of partials + one ticket per KV head must fit, else the call
-//     returns YLM_UNSUPPORTED;
+//   - scratch is YLM_NOALLOC_SCRATCH_BYTES (2 MiB). The cluster kernel (the
+//     path on B200) needs only the 256-byte step state; the split-K kernel
+//     (where cluster launches are unavailable, or forced with
+//     ylm_set_attention_path) also needs hq x splits x 130 floats of partials
+//     and one ticket per KV head, and shapes whose partials do not fit return
+//     YLM_UNSUPPORTED. With at most 8 query heads per KV head and about two
+//     CTAs per SM over the KV heads, that limit is reached only past ~4000
+//     query heads;
 //   - every call shares the array, so calls that overlap on the GPU (different
 //     streams, or other threads) race; serialise them;
 //   - the array keeps the previous call's contents: the tickets are cleared and
@@ -93,30 +98,32 @@ extern "C" int ylm_k_decode_attention_noalloc(const void *qkv, const void *q_nor
     const int splits = attn_default_splits(hkv, sms);
     static_assert(sizeof(StepState) <= 256, "step state must fit its 256-byte slot");
     const size_t state_bytes = 256; // StepState, padded to the array's alignment
-    const size_t part_bytes = attn_partial_floats(hq, splits) * sizeof(float);
-    const size_t need = state_bytes + part_bytes + sizeof(int) * (size_t)hkv;
+    // the kernels' shared-memory settings and the attention path, once per
+    // device (no allocation)
+    if (prepare_device() != cudaSuccess)
+        return YLM_CUDA_ERROR;
+    const bool split_kernel = attn_uses_split_kernel();
+    const size_t part_bytes = split_kernel ? attn_partial_floats(hq, splits) * sizeof(float) : 0;
+    const size_t need = state_bytes + part_bytes + (split_kernel ? sizeof(int) * (size_t)hkv : 0);
     if (need > YLM_NOALLOC_SCRATCH_BYTES)
+    {
+        set_last_error("split-K partials exceed the fixed 2 MiB scratch");
         return YLM_UNSUPPORTED; // hq x splits too large for the fixed scratch
+    }
     void *base = nullptr;
     if (scratch_address(&base) != cudaSuccess)
         return YLM_CUDA_ERROR;
-    // the kernels' shared-memory settings, once per device (no allocation)
-    static bool prepared[64] = {};
-    if (!prepared[dev])
-    {
-        if (kernels_prepare() != cudaSuccess)
-            return YLM_CUDA_ERROR;
-        prepared[dev] = true;
-    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // an error left by an unrelated earlier runtime call must not be taken
-    // for this call's launch error
-    const cudaError_t stale = cudaGetLastError();
+    // an error left pending by an unrelated earlier runtime call is only named
+    // in this call's message (peeked, so the caller still sees it)
+    const cudaError_t stale = cudaPeekAtLastError();
     StepState *state = static_cast<StepState *>(base);
     float *partial = reinterpret_cast<float *>(static_cast<char *>(base) + state_bytes);
     int *tickets = reinterpret_cast<int *>(static_cast<char *>(base) + state_bytes + part_bytes);
-    noalloc_reset_kernel<<<1, 1, 0, s>>>(state, tickets, hkv, slot, rope_pos);
-    cudaError_t le = cudaGetLastError();
+    // launched through the runtime call that returns this launch's own status
+    int n_tickets = split_kernel ? hkv : 0;
+    void *rargs[] = {&state, &tickets, &n_tickets, &slot, &rope_pos};
+    cudaError_t le = cudaLaunchKernel((const void *)noalloc_reset_kernel, dim3(1), dim3(1), rargs, 0, s);
     if (le != cudaSuccess)
     {
         char msg[160];

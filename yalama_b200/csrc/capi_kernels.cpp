@@ -28,14 +28,19 @@ int sm_count()
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? YLM_OK : YLM_CUDA_ERROR; }
 
+} // namespace
+
+namespace ylm {
 // shared-memory opt-in of the kernels, once per device
 cudaError_t prepare_device()
 {
+    static std::mutex mu;
     static bool done[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= 64)
         return e != cudaSuccess ? e : cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
     if (!done[dev])
     {
         e = kernels_prepare();
@@ -45,10 +50,17 @@ cudaError_t prepare_device()
     }
     return cudaSuccess;
 }
-
-} // namespace
+} // namespace ylm
 
 extern "C" {
+
+int ylm_set_attention_path(int32_t split_kernel)
+{
+    if (split_kernel != 0 && split_kernel != 1)
+        return YLM_INVALID_ARG;
+    attn_force_split_kernel(split_kernel != 0);
+    return YLM_OK;
+}
 
 int ylm_k_gemv(const void *w, int32_t n, int32_t k, const void *x, void *y, void *stream)
 {

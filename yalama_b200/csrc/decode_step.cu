@@ -354,6 +354,8 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
         // then this CTA sums its rows over all ranks' slots of its own mailbox,
         // in rank order, and adds the residual, identically on every rank
         uint32_t *const *mb = a.mb[p.mbox - 1];
+        const bool stamp = a.xstat && blockIdx.x == 0 && tid == 0;
+        const uint64_t ts0 = stamp ? globaltimer_ns() : 0;
         for (int r = tid; r < t.rows; r += DS_THREADS)
         {
             float y = 0.f;
@@ -372,6 +374,11 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
             const __half v = f2h(h2f(xr[r]) + rh(sum));
             xr[r] = v;
             p.resid_t[t.r0 + r] = ds_tagged(tag, v);
+        }
+        if (stamp)
+        {
+            a.xstat[0] += globaltimer_ns() - ts0;
+            a.xstat[1] += 1ull;
         }
         return;
     }

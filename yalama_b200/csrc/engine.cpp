@@ -310,6 +310,8 @@ struct ylm_engine
     std::vector<void *> ds_mb_peer;                  // peers' mailboxes mapped through CUDA IPC
     uint32_t *ds_xt = nullptr, *ds_actt = nullptr; // tagged residual stream and SwiGLU activations
     unsigned *ds_gen = nullptr;
+    unsigned long long *ds_xstat = nullptr; // exchange timing (tensor parallel): ns, exchanges
+    int64_t xstat_steps = 0;                // decode steps since the last reset of ds_xstat
     std::vector<DsArgs> ds_seg;
 
     bool ready = false;
@@ -360,7 +362,7 @@ struct ylm_engine
                         (void *)qkv, (void *)att, (void *)act, (void *)logits, (void *)logits_local, (void *)ar,
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
-                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen})
+                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen, (void *)ds_xstat})
             // logits_local is logits itself without tensor parallelism: free once
             if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
@@ -817,7 +819,11 @@ struct ylm_engine
         d.tp = tp;
         d.rank = rank;
         if (tp > 1)
+        {
             setup_mailboxes(d);
+            ds_xstat = dalloc<unsigned long long>(2);
+            d.xstat = ds_xstat;
+        }
         d.eps = cfg.rms_eps;
         d.emb = emb;
         d.vocab = V;
@@ -1085,6 +1091,7 @@ struct ylm_engine
 
     void launch_forward(bool sample)
     {
+        xstat_steps++;
         if (ds_on && opt.use_cuda_graph && ds_graph_ok)
         {
             cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
@@ -1846,6 +1853,99 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
         e->pull_state_sync();
         *ms_per_launch = ms / iters;
         *weight_bytes = bytes;
+        return YLM_OK;
+    });
+}
+
+int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *exchanges, double *steps)
+{
+    return guarded([&]() -> int {
+        if (!e)
+            fail(YLM_INVALID_ARG, "null engine");
+        CK(cudaSetDevice(e->dev));
+        unsigned long long v[2] = {0, 0};
+        if (e->ds_xstat)
+        {
+            CK(cudaStreamSynchronize(e->st));
+            CK(cudaMemcpy(v, e->ds_xstat, sizeof(v), cudaMemcpyDeviceToHost));
+        }
+        if (wait_ms)
+            *wait_ms = (double)v[0] * 1e-6;
+        if (exchanges)
+            *exchanges = (double)v[1];
+        if (steps)
+            *steps = (double)e->xstat_steps;
+        if (reset)
+        {
+            if (e->ds_xstat)
+                CK(cudaMemset(e->ds_xstat, 0, sizeof(v)));
+            e->xstat_steps = 0;
+        }
+        return YLM_OK;
+    });
+}
+
+int ylm_time_allreduce(ylm_engine *e, int32_t iters, double *ms_per_step)
+{
+    return guarded([&]() -> int {
+        if (!e || iters <= 0 || !ms_per_step)
+            fail(YLM_INVALID_ARG, "bad argument");
+        if (e->tp <= 1)
+            return (int)YLM_UNSUPPORTED;
+        CK(cudaSetDevice(e->dev));
+        // the decode step's collectives: 2L all-reduces of [hidden] FP16, back
+        // to back in one graph (the per-op path's exchange, without the GEMVs)
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ex = nullptr;
+        CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+        ncclResult_t nr = ncclSuccess;
+        for (int i = 0; i < 2 * e->L && nr == ncclSuccess; i++)
+            nr = ncclAllReduce(e->ar, e->ar, e->H, ncclHalf, ncclSum, e->comm, e->st);
+        cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+        if (nr != ncclSuccess || ce != cudaSuccess)
+        {
+            if (g)
+                cudaGraphDestroy(g);
+            NK(nr);
+            CK(ce);
+        }
+        ce = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        CK(ce);
+        cudaEvent_t a = nullptr, b = nullptr;
+        float ms = 0;
+        auto run = [&]() {
+            CK(cudaGraphLaunch(ex, e->st)); // warm
+            NK(ncclAllReduce(e->ar, e->ar, 1, ncclHalf, ncclSum, e->comm, e->st));
+            CK(cudaEventCreate(&a));
+            CK(cudaEventCreate(&b));
+            CK(cudaEventRecord(a, e->st));
+            for (int i = 0; i < iters; i++)
+                CK(cudaGraphLaunch(ex, e->st));
+            CK(cudaEventRecord(b, e->st));
+            CK(cudaEventSynchronize(b));
+            CK(cudaEventElapsedTime(&ms, a, b));
+        };
+        try
+        {
+            run();
+        }
+        catch (...)
+        {
+            cudaStreamSynchronize(e->st);
+            cudaGraphExecDestroy(ex);
+            if (a)
+                cudaEventDestroy(a);
+            if (b)
+                cudaEventDestroy(b);
+            throw;
+        }
+        cudaGraphExecDestroy(ex); // a graph holding NCCL calls must not outlive the communicator
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        CK(cudaMemsetAsync(e->ar, 0, sizeof(__half) * e->H, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        *ms_per_step = ms / iters;
         return YLM_OK;
     });
 }

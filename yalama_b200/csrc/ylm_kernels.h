@@ -111,6 +111,10 @@ size_t attn_partial_floats(int hq, int splits);
 int attn_default_splits(int hkv, int num_sms);
 cudaError_t attn_decode_launch(const AttnArgs &a, cudaStream_t s, bool pdl);
 cudaError_t attn_prepare();
+// Process-wide: launch the split-K kernel (global partials, tickets) even where
+// cluster launches are available; whether later launches use it.
+void attn_force_split_kernel(bool on);
+bool attn_uses_split_kernel();
 
 // ------------------------------------------------------------------ sampler
 struct SampleArgs
@@ -173,6 +177,10 @@ struct DsArgs
     // into this process (peer memory over NVLink for q != rank)
     int tp, rank;
     uint32_t *mb[2][8];
+    // exchange timing (tensor parallel, may be null): [0] += ns from block 0
+    // thread 0's first partial store to the arrival of every rank's partial of
+    // its row, [1] += 1, per exchange
+    unsigned long long *xstat;
     int tab_bytes;  // shared-memory layout: phase table, work area, residual rows
     int work_bytes; // GEMV input vector, partials, RMSNorm scratch
     int kpad_max;   // largest input vector (halves, multiple of the task width)
@@ -187,6 +195,8 @@ cudaError_t ds_launch(const DsArgs &a, size_t smem, int grid, cudaStream_t s);
 
 // Shared-memory opt-in of every kernel on the current device (idempotent).
 cudaError_t kernels_prepare();
+// kernels_prepare() once per device, thread-safe (the kernel-level entry points).
+cudaError_t prepare_device();
 
 // Message returned by ylm_last_error() on the calling thread (kernel-level entry points).
 void set_last_error(const char *msg);

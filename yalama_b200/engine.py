@@ -143,6 +143,9 @@ SIGNATURES = {
     "ylm_last_prefill_ms": (ctypes.c_int, [_P, _F64P]),
     "ylm_decode_path": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_int32)]),
     "ylm_time_segment": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _F64P, _F64P]),
+    "ylm_exchange_stats": (ctypes.c_int, [_P, ctypes.c_int32, _F64P, _F64P, _F64P]),
+    "ylm_time_allreduce": (ctypes.c_int, [_P, ctypes.c_int32, _F64P]),
+    "ylm_set_attention_path": (ctypes.c_int, [ctypes.c_int32]),
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
     "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_prefill_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
@@ -171,6 +174,19 @@ def lib() -> ctypes.CDLL:
             f.argtypes = args
         _lib = L
     return _lib
+
+
+class split_attention:
+    """Context manager: the split-K decode-attention kernel for every launch
+    (and CUDA graph captured) inside the block, process-wide."""
+
+    def __enter__(self):
+        check(lib().ylm_set_attention_path(1), "ylm_set_attention_path")
+        return self
+
+    def __exit__(self, *exc):
+        lib().ylm_set_attention_path(0)
+        return False
 
 
 def check(status: int, where: str) -> None:
@@ -375,6 +391,25 @@ class Engine:
         ms, nb = ctypes.c_double(), ctypes.c_double()
         check(lib().ylm_time_segment(self._h, layer, iters, ctypes.byref(ms), ctypes.byref(nb)), "ylm_time_segment")
         return ms.value, nb.value
+
+    def exchange_stats(self, reset: bool = False) -> dict:
+        """Device time in the fused all-reduce exchanges (tensor parallel)."""
+        w, n, t = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        check(lib().ylm_exchange_stats(self._h, int(reset), ctypes.byref(w), ctypes.byref(n), ctypes.byref(t)),
+              "ylm_exchange_stats")
+        return {"wait_ms": w.value, "exchanges": n.value, "tokens": t.value}
+
+    def reset_exchange_stats(self) -> None:
+        self.exchange_stats(reset=True)
+
+    def time_allreduce(self, iters: int) -> Optional[float]:
+        """ms per decode step of the step's 2L NCCL all-reduces alone (None at tp = 1)."""
+        ms = ctypes.c_double()
+        st = lib().ylm_time_allreduce(self._h, iters, ctypes.byref(ms))
+        if st == Status.UNSUPPORTED:
+            return None
+        check(st, "ylm_time_allreduce")
+        return ms.value
 
     def decode_persistent(self) -> bool:
         """True when decode steps run as one cooperative kernel."""

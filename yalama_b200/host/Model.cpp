@@ -16,20 +16,30 @@
 // Model.cpp:29-30).
 //
 // Also provided: Model_SampleOnDevice(), the engine's on-device sampler for the
-// current logits (the replacement for ChatSession::Sample's LibTorch ops).
+// current logits (the replacement for ChatSession::Sample's LibTorch ops), and
+// Model_RecordInputs() / Model_RecordedInputs(), which keep the token ids of
+// every Infer call (off by default; tests compare them with the engine's own
+// token loop).
 #include "Model.h"
 #include "ConfigManager.h"
+#include "TraceLogger.h"
 #include "yalama_b200.h"
 
 #include <stdexcept>
 #include <string>
 #include <vector>
 
-std::unique_ptr<ModelBase> Model::_model = nullptr; // declared by Model.h; unused here
+// Model.h's private `_model` (a ModelBase) is not defined: nothing here uses it,
+// and defining it would pull ModelBase's vtable (src/models/ModelBase.cpp) into
+// the link. The step counter ChatSession advances (src/ChatSession.cpp:226) is
+// defined in ModelBase.cpp:17, which this file replaces, so it lives here.
+int TraceLogger::_TraceStep = 0;
 
 namespace
 {
 ylm_engine *g_engine = nullptr;
+bool g_record = false;
+std::vector<std::vector<int64_t>> g_inputs;
 
 [[noreturn]] void throw_status(int status, const char *where)
 {
@@ -42,8 +52,10 @@ void Model::Init()
     ylm_model_config cfg;
     const std::string cfg_path = ConfigManager::ModelPath + "/config.json";
     int st = ylm_config_from_json(cfg_path.c_str(), &cfg);
-    if (st != YLM_OK)
+    if (st == YLM_UNSUPPORTED)
         throw_status(st, "Unrecognized/unsupported model type. Supported: Llama 3+, Mistral");
+    if (st != YLM_OK)
+        throw_status(st, ("Model::Init: cannot read " + cfg_path).c_str());
     // ConfigManager has already resolved these (src/ConfigManager.cpp:410-471)
     cfg.model_type = static_cast<int32_t>(ConfigManager::ModelLoadedType);
     cfg.num_layers = ConfigManager::NumLayers;
@@ -77,6 +89,7 @@ void Model::Init()
 void Model::BeginInfer()
 {
     EnsureModelIsInitialized();
+    TraceLogger::_TraceStep = 0; // ModelBase::BeginInfer, ModelBase.cpp:298
     const int st = ylm_begin_infer(g_engine);
     if (st != YLM_OK)
         throw_status(st, "Model::BeginInfer");
@@ -89,6 +102,8 @@ GenerationResult Model::Infer(torch::Tensor &tokenVectors, std::vector<int> &eos
 
     torch::Tensor host = tokenVectors.to(torch::kCPU, torch::kInt64).contiguous().view({-1});
     std::vector<int64_t> ids(host.data_ptr<int64_t>(), host.data_ptr<int64_t>() + host.numel());
+    if (g_record)
+        g_inputs.push_back(ids);
     int32_t n = static_cast<int32_t>(ids.size());
     int32_t n_eos = static_cast<int32_t>(eosPerPrompt.size());
     std::vector<int32_t> eos(eosPerPrompt.begin(), eosPerPrompt.end());
@@ -163,3 +178,11 @@ int64_t Model_SampleOnDevice(bool greedy, const std::vector<int64_t> &masked_ids
         throw_status(st, "ylm_sample");
     return id;
 }
+
+void Model_RecordInputs(bool on)
+{
+    g_record = on;
+    g_inputs.clear();
+}
+
+const std::vector<std::vector<int64_t>> &Model_RecordedInputs() { return g_inputs; }

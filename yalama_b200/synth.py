@@ -266,14 +266,35 @@ def write_safetensors(path: str, tensors: List[Tuple[str, Tuple[int, ...], "call
             f.write(_encode(a, dtype))
 
 
+TILE_PERIOD = 16777213  # 2**24 - 3, prime
+
+
+def tiled_values(block: np.ndarray, start: int, shape: Tuple[int, ...]) -> np.ndarray:
+    """`block` read cyclically from `start` into an array of `shape` (float32)."""
+    n = int(np.prod(shape))
+    out = np.empty(n, dtype=np.float32)
+    p = block.size
+    pos, src = 0, start % p
+    while pos < n:
+        c = min(n - pos, p - src)
+        out[pos:pos + c] = block[src:src + c]
+        pos += c
+        src = 0
+    return out.reshape(shape)
+
+
 def write_snapshot(root: str, spec: ModelSpec, seed: int = 0, dtype: str = "F16",
                    std: float = 0.02, shard_bytes: int = 4 << 30, fast: bool = False,
                    snapshot_hash: str = "0000000000000000000000000000000000000000") -> str:
     """Write an HF hub layout under `root`; return the snapshot directory.
 
-    `fast=True` draws weights with numpy's PCG64 normal generator instead of
-    the counter-based one (same distribution, much faster at billions of
-    parameters); use it where only timing matters.
+    `fast=True` fills the weights from one block of ``TILE_PERIOD`` N(0, std)
+    values (numpy PCG64 from the seed), each tensor reading the block
+    cyclically from its own offset, instead of the counter-based generator:
+    the same distribution, written at disk speed for billions of parameters.
+    The period is prime, so no two rows of a power-of-two-wide (or any
+    shorter-than-the-period) matrix repeat. Use it where every consumer loads
+    the same file (timing, or parity between two loaders of the snapshot).
     """
     snap = os.path.join(root, "snapshots", snapshot_hash)
     os.makedirs(snap, exist_ok=True)
@@ -286,12 +307,14 @@ def write_snapshot(root: str, spec: ModelSpec, seed: int = 0, dtype: str = "F16"
         json.dump({"eos_token": "<eos>", "bos_token": None}, f)
 
     esize = {"F16": 2, "BF16": 2, "F32": 4}[dtype]
-    rng = np.random.default_rng(seed) if fast else None
+    block = None
+    if fast:
+        block = np.random.default_rng(seed).standard_normal(TILE_PERIOD, dtype=np.float32) * np.float32(std)
 
     def producer(name, shape):
         def make():
             if fast and not name.endswith("norm.weight"):
-                return (rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+                return tiled_values(block, fnv1a64(name) % TILE_PERIOD, shape)
             return tensor_values(seed, name, shape, std)
         return make
 
@@ -338,3 +361,110 @@ def write_ids(path: str, ids) -> None:
 def prompt_ids(seed: int, n: int, vocab: int) -> np.ndarray:
     """Prompt of n token ids uniform over [0, vocab), from the seed."""
     return np.random.default_rng(seed + 0x5EED).integers(0, vocab, size=n, dtype=np.int64)
+
+
+# ---------------------------------------------------------------------------
+# Byte-level BPE tokenizer fixture (tokenizer.json / tokenizer_config.json)
+# ---------------------------------------------------------------------------
+# Special tokens per family, as the reference's chat templates spell them
+# (include/chat_templates/*ChatTemplateProvider.h); the last one is the EOS.
+SPECIAL_TOKENS = {
+    "llama": ["<|begin_of_text|>", "<|end_of_text|>", "<|start_header_id|>", "<|end_header_id|>",
+              "<|reserved_special_token_0|>", "<|eot_id|>"],
+    "qwen": ["<|endoftext|>", "<|im_start|>", "<think>", "</think>", "<|im_end|>"],
+}
+
+_SAMPLE_TEXT = (
+    "The engine streams every weight matrix once per token, and the attention reads the cached keys "
+    "and values of the context. A persistent kernel keeps one block on each multiprocessor, so the "
+    "next projection starts while the previous one is finishing. Tokens are generated one at a time: "
+    "the model reads the prompt, then answers with the most likely word, again and again, until it "
+    "reaches the end of the text or the length limit."
+)
+
+
+def byte_alphabet() -> List[str]:
+    """The byte-level BPE alphabet: byte b -> a printable character (bytes
+    33-126, 161-172, 174-255 map to themselves, the others to 256 + n in
+    order), the mapping the reference's TokenizerBase::BuildByteEncoder
+    builds (src/tokenizer/TokenizerBase.cpp:17-63)."""
+    safe = set(range(33, 127)) | set(range(161, 173)) | set(range(174, 256))
+    out, n = [], 0
+    for b in range(256):
+        if b in safe:
+            out.append(chr(b))
+        else:
+            out.append(chr(256 + n))
+            n += 1
+    return out
+
+
+def train_merges(text: str, n_merges: int) -> List[Tuple[str, str]]:
+    """Greedy BPE merges (most frequent adjacent pair first, ties by first
+    occurrence) over the words of `text` in the byte alphabet, a space
+    attached to the following word as 'Ġ'."""
+    alpha = byte_alphabet()
+    words: List[List[str]] = []
+    for i, w in enumerate(text.split(" ")):
+        b = (" " + w if i else w).encode()
+        words.append([alpha[c] for c in b])
+    merges: List[Tuple[str, str]] = []
+    for _ in range(n_merges):
+        counts: Dict[Tuple[str, str], int] = {}
+        order: Dict[Tuple[str, str], int] = {}
+        for w in words:
+            for a, b in zip(w, w[1:]):
+                counts[(a, b)] = counts.get((a, b), 0) + 1
+                order.setdefault((a, b), len(order))
+        if not counts:
+            break
+        best = max(counts, key=lambda p: (counts[p], -order[p]))
+        if counts[best] < 2:
+            break
+        merges.append(best)
+        for j, w in enumerate(words):
+            out, k = [], 0
+            while k < len(w):
+                if k + 1 < len(w) and (w[k], w[k + 1]) == best:
+                    out.append(w[k] + w[k + 1])
+                    k += 2
+                else:
+                    out.append(w[k])
+                    k += 1
+            words[j] = out
+    return merges
+
+
+def write_tokenizer(snap: str, spec: ModelSpec, family: str = "llama", n_merges: int = 200) -> Dict[str, int]:
+    """Write tokenizer.json (byte-level BPE: the 256 byte characters as ids
+    0-255, merges learned from a fixed sample text as the next ids, the
+    family's special tokens as the last ids of the vocabulary) and a
+    tokenizer_config.json naming the EOS and carrying a chat template. Returns
+    the special tokens' ids. The vocabulary fits in spec.vocab."""
+    specials = SPECIAL_TOKENS[family]
+    merges = train_merges(_SAMPLE_TEXT, n_merges)
+    vocab: Dict[str, int] = {c: i for i, c in enumerate(byte_alphabet())}
+    for a, b in merges:
+        if a + b not in vocab:
+            vocab[a + b] = len(vocab)
+    if len(vocab) + len(specials) > spec.vocab:
+        raise ValueError("vocabulary too small for the tokenizer fixture")
+    sp = {t: spec.vocab - len(specials) + i for i, t in enumerate(specials)}
+    tok = {
+        "version": "1.0",
+        "added_tokens": [{"id": i, "content": t, "single_word": False, "lstrip": False, "rstrip": False,
+                          "normalized": False, "special": True} for t, i in sp.items()],
+        "model": {"type": "BPE", "vocab": vocab, "merges": [f"{a} {b}" for a, b in merges]},
+    }
+    with open(os.path.join(snap, "tokenizer.json"), "w") as f:
+        json.dump(tok, f, ensure_ascii=False)
+    eos = specials[-1]
+    with open(os.path.join(snap, "tokenizer_config.json"), "w") as f:
+        json.dump({"eos_token": eos, "bos_token": specials[0] if family == "llama" else None,
+                   "chat_template": "{% for m in messages %}{{ m.content }}{% endfor %}"}, f)
+    cfg_path = os.path.join(snap, "config.json")
+    cfg = json.load(open(cfg_path))
+    cfg["eos_token_id"] = sp[eos]
+    with open(cfg_path, "w") as f:
+        json.dump(cfg, f, indent=1)
+    return sp
