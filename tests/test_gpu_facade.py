@@ -32,7 +32,7 @@ def test_chat_session_generate_through_facade(fam, family, tmp_path):
     specials = synth.write_tokenizer(snap, spec, family)
     eos = specials[synth.SPECIAL_TOKENS[family][-1]]
     r = subprocess.run([BIN, "--model", root, "--message", "Tell me about the engine and the tokens."],
-                       capture_output=True, text=True, timeout=600)
+                       capture_output=True, text=True, errors="replace", timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     out = json.loads(r.stdout.strip().splitlines()[-1])
     assert out["ok"], out
