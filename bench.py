@@ -329,9 +329,9 @@ def gpu_reference(spec, prompt, top_k, temp):
 def segment_roofline(eng, spec, hbm_peak, peak_kind):
     """The dominant kernel of the persistent path: one decode GEMV segment (a
     middle layer's O, gate-up, down and the next layer's QKV) timed alone with
-    CUDA events on the engine stream, back to back; its weights (436 MB for
-    the 8B shape) exceed L2, so every launch streams them from HBM.
-    Algorithmic bytes = the segment's weights."""
+    CUDA events on the engine stream, back to back; its weights (436 MB for the
+    8B shape) exceed L2, so every launch streams them from HBM. Algorithmic
+    bytes = the segment's weights."""
     ms, wbytes = eng.time_segment(spec.layers // 2, 48)
     achieved = wbytes / (ms * 1e-3) / 1e9
     return {"kernel": "decode_segment_kernel (O + gate-up + down + next QKV of one layer, FP16)",

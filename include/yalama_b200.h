@@ -94,6 +94,11 @@ typedef struct ylm_engine_options {
                                      decode step run as one persistent kernel; with tensor parallelism
                                      its O and down epilogues all-reduce over NVLink peer memory;
                                      0: the per-op graph */
+    int32_t wait_limit_us;        /* bound of every device-side wait of the persistent path (a
+                                     producer phase's tagged output, a peer's partials), in
+                                     microseconds; 0 (default): 2 s. A wait that expires records an
+                                     error, the step's remaining waits give up at once and the call
+                                     returns YLM_DEVICE_TIMEOUT; the engine stays usable. */
 } ylm_engine_options;
 
 /* ChatSession::Sample parameters (src/ChatSession.cpp:560-593). */
@@ -193,6 +198,14 @@ int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *ex
  * YLM_UNSUPPORTED without tensor parallelism. Benchmark support; no
  * counterpart in the reference. */
 int ylm_time_allreduce(ylm_engine *e, int32_t iters, double *ms_per_step);
+
+/* Test support for the bounded device waits (no counterpart in the reference):
+ * layer >= 0 makes the persistent path write that layer's SwiGLU activation
+ * (the gate-up projection's tagged output) into a scratch buffer instead, so
+ * the down projection polls words that nothing writes and its wait expires
+ * after wait_limit_us; -1 restores the step. YLM_UNSUPPORTED on the per-op
+ * path. */
+int ylm_debug_drop_output(ylm_engine *e, int32_t layer);
 
 /* Decode-attention kernel for all later launches in this process (and CUDA
  * graphs captured afterwards): 0 (default) one thread-block cluster per KV

@@ -3,6 +3,7 @@ sampling, KV-cache state machine) against the oracle's FP16-storage forward on
 the same seeded weights, through the C ABI."""
 import json
 import os
+import time
 
 import numpy as np
 import pytest
@@ -340,3 +341,76 @@ def test_llama3_scaled_rope_matches_oracle():
     eng.infer(prompt)
     _, lp = plain.infer(prompt)
     assert np.max(np.abs(eng.logits() - lp)) > 10 * LOGIT_TOL
+
+
+def test_generate_one_step_behind_stops_and_rolls_back():
+    # ylm_generate keeps one decode step in flight; a step launched past an
+    # EOS is discarded, so the cache state equals a step-by-step run's
+    spec, eng = make(FAMILIES["llama"])
+    _, ref = make(FAMILIES["llama"])
+    prompt = synth.prompt_ids(12, 32, spec.vocab)
+    ids = [int(t) for t in eng.generate(prompt, 20, eos_ids=[])["ids"]]
+    assert len(ids) == 20
+    stop = next(i for i in range(3, len(ids)) if ids[i] not in ids[:i])
+    r = eng.generate(prompt, 20, eos_ids=[ids[stop]])
+    assert r["status"] == E.Status.OK
+    assert [int(t) for t in r["ids"]] == ids[:stop]
+    assert eng.info()["last_kv_index"] == len(prompt) - 1 + stop
+    # the same tokens fed one call at a time
+    ref.begin_infer()
+    ref.infer(prompt)
+    for t in ids[:stop + 1]:
+        ref.infer([t])
+    eng.infer([ids[stop]])
+    np.testing.assert_array_equal(eng.logits(), ref.logits())
+    # max_new and the greedy ids of the per-token path (kept for a fixed draw)
+    r3 = eng.generate(prompt, 7, eos_ids=[])
+    assert [int(t) for t in r3["ids"]] == ids[:7]
+
+
+@pytest.mark.parametrize("layer", [0, 1])
+def test_device_wait_times_out_and_engine_recovers(layer):
+    # A bounded wait made to run out: the layer's SwiGLU activation goes to a
+    # scratch buffer, so the down projection polls words nothing writes.
+    # The wait gives up after wait_limit_us, the step's other waits give up at
+    # once, the call reports a device timeout, and the next request is exact.
+    spec, eng = make(FAMILIES["llama"], wait_limit_us=2000)
+    _, ref = make(FAMILIES["llama"])
+    assert eng.decode_persistent()
+    prompt = synth.prompt_ids(13, 24, spec.vocab)
+    eng.begin_infer()
+    eng.infer(prompt)
+    tok = S.greedy(eng.logits())
+    eng.debug_drop_output(layer)
+    t0 = time.time()
+    with pytest.raises(E.YlmError) as ei:
+        eng.infer([tok])
+    assert ei.value.status == E.Status.DEVICE_TIMEOUT
+    assert time.time() - t0 < 1.0  # the 2 ms bound, not the default 2 s
+    eng.debug_drop_output(-1)
+    for e in (eng, ref):
+        e.begin_infer()
+        e.infer(prompt)
+    for _ in range(3):
+        eng.infer([tok])
+        ref.infer([tok])
+        np.testing.assert_array_equal(eng.logits(), ref.logits())
+        tok = S.greedy(ref.logits())
+
+
+@pytest.mark.parametrize("fam", ["llama_g8", "qwen2"])
+def test_fused_greedy_pick_is_the_argmax(fam):
+    # one decode step + greedy sample on the persistent path picks the token in
+    # the lm_head epilogue (no sampler launch): the first index of the maximum
+    # of the FP16 logits, as torch::argmax and the sampler kernel pick it
+    spec, eng = make(FAMILIES[fam])
+    assert eng.decode_persistent()
+    eng.begin_infer()
+    eng.infer(synth.prompt_ids(14, 30, spec.vocab))
+    tok = eng.sample(True)
+    for _ in range(16):
+        st, nxt = eng.decode(tok, True)
+        assert st == E.Status.OK
+        lg = eng.logits(as_float32=False)
+        assert nxt == int(np.argmax(lg))
+        tok = nxt

@@ -112,3 +112,72 @@ def test_tp_persistent_and_per_op_match_oracle(world, tmp_path):
             worst = oracle_worst(kw, r["rows"], r["toks"])
             print(f"{fam} tp{world} {name}: max |logit diff| vs oracle = {worst:.3e}")
             assert worst < LOGIT_TOL
+
+
+# Llama-3.1-70B width, one layer: at 8 ranks each GPU holds one KV head and
+# eight query heads, 3584 of the 28672 intermediate rows, 16032 vocabulary rows
+WIDE = dict(preset="llama3.1-70b", layers=1, prompt=300, steps=6)
+
+
+def _wide_rank_main(rank, world, port, root, out_dir):
+    import dataclasses
+    import datetime
+    import torch.distributed as dist
+    from yalama_b200 import engine as E
+    from yalama_b200 import tp as TP
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300))
+    try:
+        spec = dataclasses.replace(synth.PRESETS[WIDE["preset"]], layers=WIDE["layers"])
+        snap = E.resolve_snapshot(root)
+        prompt = synth.prompt_ids(21, WIDE["prompt"], spec.vocab)
+        for persistent in (0, 1):
+            # every rank slices its share of each tensor straight from the snapshot
+            eng = TP.tp_engine(dist, rank, world, E.config_from_spec(spec), snapshot_dir=snap,
+                               decode_persistent=persistent)
+            eng.begin_infer()
+            st, _ = eng.infer(prompt)
+            assert st == E.Status.OK
+            rows, toks = [eng.logits()], []
+            for _ in range(WIDE["steps"]):
+                tok = S.greedy(rows[-1])
+                toks.append(tok)
+                st, _ = eng.infer([tok])
+                assert st == E.Status.OK
+                rows.append(eng.logits())
+            if rank == 0:
+                np.savez(os.path.join(out_dir, f"wide_{persistent}.npz"), rows=np.stack(rows), toks=np.array(toks))
+            eng.close()
+            dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_tp_snapshot_slices_at_70b_width(world, tmp_path):
+    if gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import dataclasses
+    import torch.multiprocessing as mp
+    from yalama_b200 import engine as E
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    spec = dataclasses.replace(synth.PRESETS[WIDE["preset"]], layers=WIDE["layers"])
+    root = str(tmp_path / "model")
+    synth.write_snapshot(root, spec, seed=0, dtype="F16", fast=True)
+    mp.start_processes(_wide_rank_main, args=(world, free_port(), root, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    # the same snapshot on one GPU, fed the same tokens
+    one = E.Engine(E.resolve_snapshot(root), E.config_from_spec(spec), device=0)
+    prompt = synth.prompt_ids(21, WIDE["prompt"], spec.vocab)
+    for persistent in (0, 1):
+        z = np.load(tmp_path / f"wide_{persistent}.npz")
+        one.begin_infer()
+        one.infer(prompt)
+        worst = float(np.max(np.abs(one.logits() - z["rows"][0])))
+        for i, tok in enumerate(z["toks"]):
+            one.infer([int(tok)])
+            worst = max(worst, float(np.max(np.abs(one.logits() - z["rows"][i + 1]))))
+        print(f"70b width tp{world} persistent={persistent}: max |logit diff| vs one GPU = {worst:.3e}")
+        assert worst < LOGIT_TOL
+    one.close()

@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 
 // ---------------------------------------------------------------- cluster variant
 // One thread-block cluster per KV head, one CTA per split of the cached
-// tokens (S = cluster size, 16 where the device allows non-portable clusters,
-// else 8). Inside a CTA each warp takes whole tokens (lane l holds dimensions
+// tokens (S = cluster size: 8, the portable size, where the device can
+// schedule it; the kernel also supports 16). Inside a CTA each warp takes whole tokens (lane l holds dimensions
 // 4l..4l+3), ATC_UT tokens per batch: all their scores first, then one
 // rescale of the running softmax state. The 8 warp states are merged in
 // shared memory; each CTA then stores its partial (M, L and one slice of O per
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 // of the S partials and writes it. No global scratch, fence or atomic ticket.
 constexpr int ATC_THREADS = 256;
 constexpr int ATC_WARPS = ATC_THREADS / 32;
-constexpr int ATC_MAX_SPLITS = 16; // largest cluster
+constexpr int ATC_MAX_SPLITS = 16; // largest cluster the kernel supports
 constexpr int ATC_MIN_SPLITS = 8;  // smallest cluster (the portable size)
 
 static int g_cluster_splits = 0; // 16, 8, or 0 (no cluster launch: split-K kernel)
@@ -672,7 +672,10 @@ template <int G> static cudaError_t attn_prepare_t()
 
 cudaError_t attn_prepare()
 {
-    int S = 16;
+    // 8-CTA clusters: at the Llama-3.1-8B shape (8 KV heads, 2-3k cached
+    // tokens) a decode step measured 3.23 ms with 8-CTA clusters against 3.37
+    // with 16 (Qwen3-0.6B: 0.80 against 0.82 ms)
+    int S = 8;
     S = std::min(S, attn_cluster_prepare_t<1>());
     S = std::min(S, attn_cluster_prepare_t<2>());
     S = std::min(S, attn_cluster_prepare_t<3>());

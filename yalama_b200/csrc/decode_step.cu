@@ -34,7 +34,7 @@
 //
 // Weights, norms and the embedding are constant and use the streaming path;
 // activations are read through L2 only (ld.global.cg). Every wait is bounded
-// (YLM_WAIT_LIMIT_NS) and records YLM_DEV_ERR_TIMEOUT_PEER in the step
+// (DsArgs::wait_ns, 2 s unless the engine sets it) and records YLM_DEV_ERR_TIMEOUT_PEER in the step
 // state's error word; after any recorded error the remaining waits give up at
 // once, and the host clears the tagged buffers.
 //
@@ -150,7 +150,7 @@ __device__ __forceinline__ uint32_t ds_tagged(uint32_t tag, __half v)
 }
 
 // 8 tagged words at w (16-byte aligned) -> 8 halves, once every tag is `want`.
-// Bounded: after YLM_WAIT_LIMIT_NS, or at once after any recorded error, the
+// Bounded: after a.wait_ns, or at once after any recorded error, the
 // current words are used.
 __device__ __forceinline__ uint4 ds_read_tagged8(const DsArgs &a, const uint32_t *w, uint32_t want)
 {
@@ -176,7 +176,7 @@ __device__ __forceinline__ uint4 ds_read_tagged8(const DsArgs &a, const uint32_t
             {
                 if (*reinterpret_cast<volatile int *>(a.err) != 0)
                     break;
-                if (globaltimer_ns() - t0 > YLM_WAIT_LIMIT_NS)
+                if (globaltimer_ns() - t0 > a.wait_ns)
                 {
                     atomicExch(a.err, YLM_DEV_ERR_TIMEOUT_PEER);
                     break;
@@ -209,7 +209,7 @@ __device__ __forceinline__ __half ds_read_tagged1(const DsArgs &a, const uint32_
             {
                 if (*reinterpret_cast<volatile int *>(a.err) != 0)
                     break;
-                if (globaltimer_ns() - t0 > YLM_WAIT_LIMIT_NS)
+                if (globaltimer_ns() - t0 > a.wait_ns)
                 {
                     atomicExch(a.err, YLM_DEV_ERR_TIMEOUT_PEER);
                     break;
@@ -325,6 +325,65 @@ __device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, i
     named_bar_sync(1, DS_THREADS);
 }
 
+// Greedy sampling fused into the lm_head epilogue (ChatSession::Sample's
+// argmax, src/ChatSession.cpp:564-567; the sampler kernel's greedy path):
+// the CTA's best key to pick_cand, then the last CTA to arrive takes the
+// maximum over all CTAs and updates the step state as the sampler does.
+__shared__ uint64_t ds_pick[DS_WARPS];
+__shared__ int ds_pick_last;
+
+// (out of line with its three pointers by value: a reference to the kernel
+// parameters would copy them all to the stack)
+__device__ __noinline__ void ds_greedy_pick(StepState *state, unsigned long long *cand, int *counter, uint64_t best,
+                                            int tid)
+{
+    const int warp = tid >> 5, lane = tid & 31;
+    best = warp_max_u64(best);
+    if (lane == 0)
+        ds_pick[warp] = best;
+    named_bar_sync(1, DS_THREADS);
+    if (tid == 0)
+    {
+        uint64_t b = 0;
+        for (int w = 0; w < DS_WARPS; w++)
+            b = ds_pick[w] > b ? ds_pick[w] : b;
+        cand[blockIdx.x] = b;
+        __threadfence();
+        ds_pick_last = atomicAdd(counter, 1) == (int)gridDim.x - 1;
+    }
+    named_bar_sync(1, DS_THREADS);
+    if (!ds_pick_last)
+        return;
+    __threadfence();
+    uint64_t k = 0;
+    for (int c = tid; c < (int)gridDim.x; c += DS_THREADS)
+    {
+        const uint64_t v = __ldcg(cand + c);
+        k = v > k ? v : k;
+    }
+    k = warp_max_u64(k);
+    if (lane == 0)
+        ds_pick[warp] = k;
+    named_bar_sync(1, DS_THREADS);
+    if (tid == 0)
+    {
+        uint64_t b = 0;
+        for (int w = 0; w < DS_WARPS; w++)
+            b = ds_pick[w] > b ? ds_pick[w] : b;
+        StepState *s = state;
+        const int64_t id = (int64_t)key_idx(b);
+        s->next_token = id;
+        s->sample_calls = s->sample_calls + 1;
+        if (s->advance)
+        {
+            s->token = id;
+            s->slot = s->slot + 1;
+            s->rope_pos = s->rope_pos + 1;
+        }
+        *counter = 0;
+    }
+}
+
 // Row sums of the chunk partials in order, then the epilogue of the per-op
 // kernel; activations consumed inside the launch are written tagged.
 __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, const DsTab &t, const float *part,
@@ -382,6 +441,7 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
         }
         return;
     }
+    uint64_t best = 0; // greedy_pick: this thread's best (value, index) key
     for (int r = tid; r < t.rows; r += DS_THREADS)
     {
         float y = 0.f;
@@ -392,7 +452,13 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
         {
             if (p.bias)
                 y = rh(y) + h2f(p.bias[row]);
-            p.out[row] = f2h(y);
+            const __half h = f2h(y);
+            p.out[row] = h;
+            if (p.greedy_pick)
+            {
+                const uint64_t k = make_key(ord16(__half_as_ushort(h)), (uint32_t)row);
+                best = k > best ? k : best;
+            }
         }
         else
         {
@@ -404,6 +470,8 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
             p.resid_t[row] = ds_tagged(tag, v);
         }
     }
+    if (p.greedy_pick)
+        ds_greedy_pick(a.pick_state, a.pick_cand, a.pick_counter, best, tid);
 }
 
 // Task cursor of one warp through the phases of a launch: phase, row, chunk,

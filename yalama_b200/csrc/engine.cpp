@@ -297,6 +297,9 @@ struct ylm_engine
     int64_t *pIds = nullptr;
 
     cudaGraphExec_t g_fwd = nullptr, g_fwd_sample = nullptr;
+    cudaGraphExec_t g_fwd_greedy = nullptr; // persistent path, greedy pick fused into the lm_head
+    unsigned long long *pick_cand = nullptr; // its per-CTA keys [sms]
+    int *pick_counter = nullptr;
 
     // persistent GEMV segments (decode_step.cu): phase table, barrier counters,
     // one argument block per segment (layer 0's QKV; O, gate-up, down and the
@@ -313,6 +316,8 @@ struct ylm_engine
     unsigned long long *ds_xstat = nullptr; // exchange timing (tensor parallel): ns, exchanges
     int64_t xstat_steps = 0;                // decode steps since the last reset of ds_xstat
     std::vector<DsArgs> ds_seg;
+    std::vector<DsArgs> ds_seg_saved; // ylm_debug_drop_output: the segments as set up
+    uint32_t *ds_sink = nullptr;      // where a dropped output goes
 
     bool ready = false;
     int last = 0;
@@ -328,6 +333,8 @@ struct ylm_engine
 
     ncclComm_t comm = nullptr;
     cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+    StepState *hring[2] = {nullptr, nullptr}; // ylm_generate: step states read one step behind
+    cudaEvent_t ev_ring[2] = {nullptr, nullptr};
     double prefill_ms = 0.0;
 
     ~ylm_engine() { release(); }
@@ -340,7 +347,9 @@ struct ylm_engine
             cudaGraphExecDestroy(g_fwd);
         if (g_fwd_sample)
             cudaGraphExecDestroy(g_fwd_sample);
-        g_fwd = g_fwd_sample = nullptr;
+        if (g_fwd_greedy)
+            cudaGraphExecDestroy(g_fwd_greedy);
+        g_fwd = g_fwd_sample = g_fwd_greedy = nullptr;
         for (void *pm : ds_mb_peer)
             cudaIpcCloseMemHandle(pm);
         ds_mb_peer.clear();
@@ -358,11 +367,21 @@ struct ylm_engine
         if (ev_b)
             cudaEventDestroy(ev_b);
         ev_a = ev_b = nullptr;
+        for (int k = 0; k < 2; k++)
+        {
+            if (ev_ring[k])
+                cudaEventDestroy(ev_ring[k]);
+            if (hring[k])
+                cudaFreeHost(hring[k]);
+            ev_ring[k] = nullptr;
+            hring[k] = nullptr;
+        }
         for (void *p : {(void *)wblob, (void *)kc, (void *)vc, (void *)rcos, (void *)rsin, (void *)x, (void *)x2,
                         (void *)qkv, (void *)att, (void *)act, (void *)logits, (void *)logits_local, (void *)ar,
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
-                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen, (void *)ds_xstat})
+                        (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen, (void *)ds_xstat,
+                        (void *)ds_sink, (void *)pick_cand, (void *)pick_counter})
             // logits_local is logits itself without tensor parallelism: free once
             if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
@@ -378,13 +397,34 @@ struct ylm_engine
         st = nullptr;
     }
 
+    // Every engine buffer is used on the engine stream `st`, a non-blocking
+    // stream: work on the legacy default stream (plain cudaMemset, cudaMemcpy)
+    // is not ordered before it. So buffers are zeroed, and host data is copied
+    // in, on `st` itself. (A zeroing on the default stream once raced the first
+    // prefill of a new size, whose workspace it had just allocated.)
     template <typename T> T *dalloc(size_t n)
     {
         void *p = nullptr;
         CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
-        CK(cudaMemset(p, 0, std::max<size_t>(n, 1) * sizeof(T)));
+        CK(cudaMemsetAsync(p, 0, std::max<size_t>(n, 1) * sizeof(T), st));
         return static_cast<T *>(p);
     }
+
+    // host -> device on the engine stream, complete on return (the source may be
+    // pageable or reused right after)
+    void h2d(void *dst, const void *src, size_t bytes)
+    {
+        CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st));
+        CK(cudaStreamSynchronize(st));
+    }
+
+    // device -> host on the engine stream, after the work already queued on it
+    void d2h(void *dst, const void *src, size_t bytes)
+    {
+        CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+    }
+
 
     // -------------------------------------------------------------- set-up
     void init(const char *snapshot_dir, const ylm_model_config &c, const ylm_engine_options &o)
@@ -440,6 +480,7 @@ struct ylm_engine
         build_rope();
         alloc_workspace();
         setup_persistent();
+        CK(cudaStreamSynchronize(st));
         compute_max_seq();
         CK(cudaStreamSynchronize(st));
     }
@@ -603,7 +644,8 @@ struct ylm_engine
             const uint8_t *src = t->data + ((size_t)p.r0 * cols + p.c0) * es;
             if (dc == 0)
             {
-                CK(cudaMemcpy2D(p.dst, p.ld * 2, src, cols * 2, p.nc * 2, p.nr, cudaMemcpyHostToDevice));
+                CK(cudaMemcpy2DAsync(p.dst, p.ld * 2, src, cols * 2, p.nc * 2, p.nr, cudaMemcpyHostToDevice, st));
+                CK(cudaStreamSynchronize(st));
                 continue;
             }
             // BF16 / F32 shards: convert on the host, one row band at a time
@@ -626,8 +668,9 @@ struct ylm_engine
                             memcpy(&f, e, 4);
                         stage[(size_t)i * p.nc + j] = __float2half_rn(f);
                     }
-                CK(cudaMemcpy2D(p.dst + (size_t)r * p.ld, p.ld * 2, stage.data(), p.nc * 2, p.nc * 2, nr,
-                                cudaMemcpyHostToDevice));
+                CK(cudaMemcpy2DAsync(p.dst + (size_t)r * p.ld, p.ld * 2, stage.data(), p.nc * 2, p.nc * 2, nr,
+                                     cudaMemcpyHostToDevice, st));
+                CK(cudaStreamSynchronize(st)); // `stage` is refilled next
             }
         }
     }
@@ -701,8 +744,8 @@ struct ylm_engine
             }
         rcos = dalloc<__half>(hc.size());
         rsin = dalloc<__half>(hs.size());
-        CK(cudaMemcpy(rcos, hc.data(), hc.size() * 2, cudaMemcpyHostToDevice));
-        CK(cudaMemcpy(rsin, hs.data(), hs.size() * 2, cudaMemcpyHostToDevice));
+        h2d(rcos, hc.data(), hc.size() * 2);
+        h2d(rsin, hs.data(), hs.size() * 2);
     }
 
     void alloc_workspace()
@@ -814,6 +857,11 @@ struct ylm_engine
             return;
         }
         ds_gen = dalloc<unsigned>(1);
+        if (tp == 1)
+        {
+            pick_cand = dalloc<unsigned long long>(C);
+            pick_counter = dalloc<int>(1);
+        }
         DsArgs d{};
         d.nph = nph;
         d.tp = tp;
@@ -832,6 +880,7 @@ struct ylm_engine
         d.hidden = H;
         d.gen = ds_gen;
         d.err = &dstate->err;
+        d.wait_ns = opt.wait_limit_us > 0 ? (unsigned long long)opt.wait_limit_us * 1000ull : 2000000000ull;
         d.tab_bytes = (int)tab_bytes;
         d.work_bytes = (int)work_bytes;
         d.kpad_max = kpad_max;
@@ -866,11 +915,11 @@ struct ylm_engine
         }
         char *dsend = dalloc<char>(sizeof(mine));
         char *drecv = dalloc<char>(sizeof(mine) * tp);
-        CK(cudaMemcpy(dsend, mine, sizeof(mine), cudaMemcpyHostToDevice));
+        h2d(dsend, mine, sizeof(mine));
         NK(ncclAllGather(dsend, drecv, sizeof(mine), ncclChar, comm, st));
         CK(cudaStreamSynchronize(st));
         std::vector<cudaIpcMemHandle_t> all(2 * (size_t)tp);
-        CK(cudaMemcpy(all.data(), drecv, sizeof(mine) * tp, cudaMemcpyDeviceToHost));
+        d2h(all.data(), drecv, sizeof(mine) * tp);
         cudaFree(dsend);
         cudaFree(drecv);
         for (int s = 0; s < 2; s++)
@@ -895,6 +944,8 @@ struct ylm_engine
         cudaMemsetAsync(ds_gen, 0, sizeof(unsigned), st);
         cudaMemsetAsync(ds_xt, 0, sizeof(uint32_t) * H, st);
         cudaMemsetAsync(ds_actt, 0, sizeof(uint32_t) * inter, st);
+        if (pick_counter)
+            cudaMemsetAsync(pick_counter, 0, sizeof(int), st);
         for (uint32_t *m : ds_mb_local)
             if (m)
                 cudaMemsetAsync(m, 0, sizeof(uint32_t) * tp * H, st);
@@ -955,13 +1006,35 @@ struct ylm_engine
         return a;
     }
 
-    void enqueue_forward(bool sample)
+    // what a decode step ends with: nothing, the sampler kernel, or (persistent
+    // path on one GPU, greedy) the argmax fused into the lm_head epilogue
+    enum { STEP_NO_SAMPLE = 0, STEP_SAMPLER = 1, STEP_GREEDY_FUSED = 2 };
+
+    int step_mode(bool sample, bool greedy) const
     {
+        if (!sample)
+            return STEP_NO_SAMPLE;
+        return greedy && ds_on && pick_counter ? STEP_GREEDY_FUSED : STEP_SAMPLER;
+    }
+
+    void enqueue_forward(int mode)
+    {
+        const bool sample = mode != STEP_NO_SAMPLE;
         if (ds_on)
         {
             // segment 0 (layer 0's QKV), then attention l and segment l + 1
             for (int l = 0; l <= L; l++)
             {
+                if (l == L && mode == STEP_GREEDY_FUSED)
+                {
+                    DsArgs d = ds_seg[l];
+                    d.ph[d.p1 - 1 - d.p0].greedy_pick = 1; // the lm_head phase
+                    d.pick_state = dstate;
+                    d.pick_cand = pick_cand;
+                    d.pick_counter = pick_counter;
+                    CK(ds_launch(d, ds_smem, sms, st));
+                    return;
+                }
                 CK(ds_launch(ds_seg[l], ds_smem, sms, st));
                 if (l < L)
                     CK(attn_decode_launch(attn_args(l), st, false));
@@ -1066,13 +1139,13 @@ struct ylm_engine
         return s;
     }
 
-    cudaGraphExec_t capture(bool sample)
+    cudaGraphExec_t capture(int mode)
     {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
         try
         {
-            enqueue_forward(sample);
+            enqueue_forward(mode);
         }
         catch (...)
         {
@@ -1089,17 +1162,24 @@ struct ylm_engine
         return ex;
     }
 
-    void launch_forward(bool sample)
+    cudaGraphExec_t &graph_for(int mode)
+    {
+        return mode == STEP_GREEDY_FUSED ? g_fwd_greedy : (mode == STEP_SAMPLER ? g_fwd_sample : g_fwd);
+    }
+
+    // one decode step; `greedy`: the sample (if any) is an argmax
+    void launch_forward(bool sample, bool greedy = false)
     {
         xstat_steps++;
+        const int mode = step_mode(sample, greedy);
         if (ds_on && opt.use_cuda_graph && ds_graph_ok)
         {
-            cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
+            cudaGraphExec_t &ex = graph_for(mode);
             if (!ex)
             {
                 try
                 {
-                    ex = capture(sample);
+                    ex = capture(mode);
                 }
                 catch (...)
                 {
@@ -1117,18 +1197,18 @@ struct ylm_engine
         }
         if (ds_on)
         {
-            enqueue_forward(sample);
+            enqueue_forward(mode);
             return;
         }
         if (opt.use_cuda_graph)
         {
-            cudaGraphExec_t &ex = sample ? g_fwd_sample : g_fwd;
+            cudaGraphExec_t &ex = graph_for(mode);
             if (!ex)
-                ex = capture(sample);
+                ex = capture(mode);
             CK(cudaGraphLaunch(ex, st));
         }
         else
-            enqueue_forward(sample);
+            enqueue_forward(mode);
     }
 
     void fill_state(int64_t token, int slot, int pos, bool do_greedy, int advance)
@@ -1150,6 +1230,18 @@ struct ylm_engine
 
     void push_state() { CK(cudaMemcpyAsync(dstate, hin, sizeof(StepState), cudaMemcpyHostToDevice, st)); }
 
+    void ensure_ring()
+    {
+        for (int k = 0; k < 2; k++)
+        {
+            if (!hring[k])
+                CK(cudaMallocHost(&hring[k], sizeof(StepState)));
+            if (!ev_ring[k])
+                CK(cudaEventCreateWithFlags(&ev_ring[k], cudaEventDisableTiming));
+        }
+    }
+
+
     void pull_state_sync()
     {
         CK(cudaMemcpyAsync(hout, dstate, sizeof(StepState), cudaMemcpyDeviceToHost, st));
@@ -1166,7 +1258,7 @@ struct ylm_engine
             cudaMemsetAsync(counters, 0, sizeof(int) * hkv, st);
             cudaMemsetAsync(smp_counter, 0, sizeof(int), st);
             if (ds_gen)
-                ds_reset();
+                ds_reset(); // (clears the fused pick's counter too)
             cudaStreamSynchronize(st);
             if (e == YLM_DEV_ERR_BAD_TOKEN)
                 fail(YLM_INVALID_ARG, "token id out of range");
@@ -1378,7 +1470,7 @@ struct ylm_engine
             fail(YLM_SEQUENCE_LENGTH_EXCEEDED, "position beyond the RoPE table");
         fill_state(id, slot, pos, do_greedy, 0);
         push_state();
-        launch_forward(true);
+        launch_forward(true, do_greedy);
         pull_state_sync();
         last++;
         has_logits = true;
@@ -1660,7 +1752,7 @@ int ylm_set_sampling(ylm_engine *e, const ylm_sampling *s)
                     bits[id >> 5] |= 1u << (id & 31);
             }
             e->mask_bits = e->dalloc<uint32_t>(bits.size());
-            CK(cudaMemcpy(e->mask_bits, bits.data(), bits.size() * 4, cudaMemcpyHostToDevice));
+            e->h2d(e->mask_bits, bits.data(), bits.size() * 4);
         }
         // the graph with the sampler bakes in the mask pointer: rebuild it
         if (e->g_fwd_sample)
@@ -1701,6 +1793,7 @@ int ylm_generate(ylm_engine *e, const int64_t *prompt, int32_t n_prompt, int32_t
             fail(YLM_INVALID_ARG, "bad argument");
         CK(cudaSetDevice(e->dev));
         using clk = std::chrono::steady_clock;
+        auto ms_since = [](clk::time_point a) { return std::chrono::duration<double, std::milli>(clk::now() - a).count(); };
         *n_out = 0;
         double t_first = 0, t_dec = 0;
         e->begin();
@@ -1709,48 +1802,161 @@ int ylm_generate(ylm_engine *e, const int64_t *prompt, int32_t n_prompt, int32_t
         int64_t next = -1;
         int status = YLM_OK;
         const bool kv = e->opt.kv_cache_enabled != 0;
-        while (generated < max_new)
+        auto finish = [&]() {
+            if (first_ms)
+                *first_ms = t_first;
+            if (decode_ms)
+                *decode_ms = t_dec;
+            return status;
+        };
+        // stop rules of ChatSession.cpp:151-161: an EOS id, or prompt + generated
+        // reaching MaxSequenceLength; the token that ends the loop is not emitted
+        auto ends = [&](int64_t tok) {
+            return std::find(eos_ids, eos_ids + n_eos, tok) != eos_ids + n_eos || n_prompt + generated >= e->max_seq;
+        };
+        if (max_new == 0)
+            return finish();
+
+        // the first token: prefill + greedy sample (ChatSession.cpp:140)
+        auto t0 = clk::now();
         {
-            auto t0 = clk::now();
-            int r;
-            if (generated == 0 || !kv || e->last == 0)
-            {
-                int32_t n = (int32_t)ids.size();
-                r = e->infer(ids.data(), &n, nullptr, nullptr);
-                ids.resize(n);
-                if (r == YLM_OK)
-                    next = e->sample(e->greedy || generated == 0); // ChatSession.cpp:140
-            }
-            else
-                r = e->decode(next, e->greedy != 0, &next);
-            auto t1 = clk::now();
-            if (r != YLM_OK)
-            {
-                status = r;
-                break;
-            }
-            const double dt = std::chrono::duration<double, std::milli>(t1 - t0).count();
-            if (generated == 0)
-                t_first = dt;
-            else
-                t_dec += dt;
-            generated++;
-            // stop rules of ChatSession.cpp:151-161: an EOS id, or prompt + generated
-            // reaching MaxSequenceLength; the token that ends the loop is not emitted
-            bool end = std::find(eos_ids, eos_ids + n_eos, next) != eos_ids + n_eos;
-            if (!end && n_prompt + generated >= e->max_seq)
-                end = true;
-            if (end)
-                break;
-            out_ids[(*n_out)++] = next;
-            if (!kv)
-                ids.push_back(next);
+            int32_t n = (int32_t)ids.size();
+            status = e->infer(ids.data(), &n, nullptr, nullptr);
+            ids.resize(n);
+            if (status != YLM_OK)
+                return finish();
+            next = e->sample(true);
         }
-        if (first_ms)
-            *first_ms = t_first;
-        if (decode_ms)
-            *decode_ms = t_dec;
-        return status;
+        t_first = ms_since(t0);
+        generated = 1;
+        if (ends(next))
+            return finish();
+        out_ids[(*n_out)++] = next;
+        if (!kv)
+            ids.push_back(next);
+
+        if (!kv || e->last == 0 || e->u_next >= 0.f || !e->opt.use_cuda_graph)
+        {
+            // one synchronous call per token: the KV cache disabled (every call
+            // a prefill), a one-token prompt (ModelBase.cpp:539-547), or a test's
+            // fixed uniform for the next draw
+            while (generated < max_new)
+            {
+                t0 = clk::now();
+                int r;
+                if (!kv || e->last == 0)
+                {
+                    int32_t n = (int32_t)ids.size();
+                    r = e->infer(ids.data(), &n, nullptr, nullptr);
+                    ids.resize(n);
+                    if (r == YLM_OK)
+                        next = e->sample(e->greedy != 0);
+                }
+                else
+                    r = e->decode(next, e->greedy != 0, &next);
+                if (r != YLM_OK)
+                {
+                    status = r;
+                    break;
+                }
+                t_dec += ms_since(t0);
+                generated++;
+                if (ends(next))
+                    break;
+                out_ids[(*n_out)++] = next;
+                if (!kv)
+                    ids.push_back(next);
+            }
+            return finish();
+        }
+
+        // Later tokens, one step in flight ahead of the host: each decode step
+        // runs in the device's advance mode (its sampler writes the next input
+        // token and moves the slot and RoPE position on), so step s + 1 is
+        // launched before the host reads step s's token; the host-side checks of
+        // a token overlap the next step. A step launched past the end (an EOS)
+        // is rolled back: its KV slot is beyond `last` and is written again by
+        // the next call that reaches it.
+        e->ensure_ring();
+        const bool greedy = e->greedy != 0;
+        // the capacity rule (ModelBase.cpp:853-866) and the RoPE table, checked
+        // for the step that would follow `last`
+        auto step_fits = [&](int *why) {
+            if (e->last + 1 > e->cap - e->last)
+            {
+                *why = YLM_KV_CACHE_EXCEEDED;
+                return false;
+            }
+            const int pos = e->opt.rope_compat ? e->last : e->last + 1;
+            if (pos >= e->max_pos)
+            {
+                *why = YLM_SEQUENCE_LENGTH_EXCEEDED;
+                return false;
+            }
+            return true;
+        };
+        auto launch = [&](int k) {
+            e->launch_forward(true, greedy);
+            CK(cudaMemcpyAsync(e->hring[k & 1], e->dstate, sizeof(StepState), cudaMemcpyDeviceToHost, e->st));
+            CK(cudaEventRecord(e->ev_ring[k & 1], e->st));
+            e->last++;
+            e->note_sample(greedy);
+        };
+        int why = YLM_OK;
+        if (!step_fits(&why))
+        {
+            status = why;
+            if (why == YLM_SEQUENCE_LENGTH_EXCEEDED)
+                fail(why, "position beyond the RoPE table");
+            return finish();
+        }
+        e->fill_state(next, e->last + 1, e->opt.rope_compat ? e->last : e->last + 1, greedy, 1);
+        e->push_state();
+        auto t_prev = clk::now();
+        launch(0);
+        for (int k = 0;; k++)
+        {
+            // step k + 1 goes out before step k's token is read, if it may follow
+            why = YLM_OK;
+            const bool more = generated + 1 < max_new && n_prompt + generated + 1 < e->max_seq && step_fits(&why);
+            if (more)
+                launch(k + 1);
+            CK(cudaEventSynchronize(e->ev_ring[k & 1]));
+            *e->hout = *e->hring[k & 1];
+            if (e->hout->err != 0)
+            {
+                cudaStreamSynchronize(e->st);
+                e->check_dev_err(); // throws
+            }
+            next = e->hout->next_token;
+            t_dec += ms_since(t_prev);
+            t_prev = clk::now();
+            generated++;
+            if (ends(next))
+            {
+                if (more)
+                {
+                    // discard the step launched past the end
+                    CK(cudaStreamSynchronize(e->st));
+                    e->last--;
+                    e->calls--;
+                }
+                break;
+            }
+            out_ids[(*n_out)++] = next;
+            if (!more)
+            {
+                if (why != YLM_OK && generated < max_new)
+                {
+                    status = why;
+                    if (why == YLM_SEQUENCE_LENGTH_EXCEEDED)
+                        fail(why, "position beyond the RoPE table");
+                }
+                break;
+            }
+        }
+        e->has_logits = true;
+        return finish();
     });
 }
 
@@ -1775,9 +1981,9 @@ int ylm_last_topk(ylm_engine *e, int64_t *ids, float *probs, int32_t *k, float *
         if (e->last_k > 0)
         {
             if (ids)
-                CK(cudaMemcpy(ids, e->dbg_ids, sizeof(int64_t) * e->last_k, cudaMemcpyDeviceToHost));
+                e->d2h(ids, e->dbg_ids, sizeof(int64_t) * e->last_k);
             if (probs)
-                CK(cudaMemcpy(probs, e->dbg_probs, sizeof(float) * e->last_k, cudaMemcpyDeviceToHost));
+                e->d2h(probs, e->dbg_probs, sizeof(float) * e->last_k);
         }
         return YLM_OK;
     });
@@ -1857,6 +2063,47 @@ int ylm_time_segment(ylm_engine *e, int32_t layer, int32_t iters, double *ms_per
     });
 }
 
+int ylm_debug_drop_output(ylm_engine *e, int32_t layer)
+{
+    return guarded([&]() -> int {
+        if (!e)
+            fail(YLM_INVALID_ARG, "null engine");
+        if (!e->ds_on)
+            return (int)YLM_UNSUPPORTED;
+        if (layer >= e->L)
+            fail(YLM_INVALID_ARG, "layer out of range");
+        CK(cudaSetDevice(e->dev));
+        CK(cudaStreamSynchronize(e->st));
+        if (e->ds_seg_saved.empty())
+            e->ds_seg_saved = e->ds_seg;
+        e->ds_seg = e->ds_seg_saved;
+        if (layer >= 0)
+        {
+            // the SwiGLU activation of `layer`, which the down projection polls
+            if (!e->ds_sink)
+                e->ds_sink = e->dalloc<uint32_t>(e->inter);
+            bool done = false;
+            for (DsArgs &d : e->ds_seg)
+                for (int i = d.p0; i < d.p1 && !done; i++)
+                    if (d.ph[i - d.p0].epi == EPI_SWIGLU && d.ph[i - d.p0].w == e->layers[layer].wgu)
+                    {
+                        d.ph[i - d.p0].out_t = e->ds_sink;
+                        done = true;
+                    }
+            if (!done)
+                fail(YLM_INVALID_ARG, "no gate-up phase for layer %d", layer);
+        }
+        // the captured graphs hold the segments' arguments: capture again
+        for (cudaGraphExec_t *g : {&e->g_fwd, &e->g_fwd_sample, &e->g_fwd_greedy})
+            if (*g)
+            {
+                cudaGraphExecDestroy(*g);
+                *g = nullptr;
+            }
+        return YLM_OK;
+    });
+}
+
 int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *exchanges, double *steps)
 {
     return guarded([&]() -> int {
@@ -1867,7 +2114,7 @@ int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *ex
         if (e->ds_xstat)
         {
             CK(cudaStreamSynchronize(e->st));
-            CK(cudaMemcpy(v, e->ds_xstat, sizeof(v), cudaMemcpyDeviceToHost));
+            e->d2h(v, e->ds_xstat, sizeof(v));
         }
         if (wait_ms)
             *wait_ms = (double)v[0] * 1e-6;
@@ -1878,7 +2125,7 @@ int ylm_exchange_stats(ylm_engine *e, int32_t reset, double *wait_ms, double *ex
         if (reset)
         {
             if (e->ds_xstat)
-                CK(cudaMemset(e->ds_xstat, 0, sizeof(v)));
+                CK(cudaMemsetAsync(e->ds_xstat, 0, sizeof(v), e->st));
             e->xstat_steps = 0;
         }
         return YLM_OK;
@@ -1966,9 +2213,10 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
         e->hin->token = e->hout->next_token >= 0 ? e->hout->next_token : 0;
         e->push_state();
         // the first launch captures the graph (outside the timed region)
-        if (!e->g_fwd_sample && e->opt.use_cuda_graph && (!e->ds_on || e->ds_graph_ok))
+        const bool greedy = e->greedy != 0;
+        if (!e->graph_for(e->step_mode(true, greedy)) && e->opt.use_cuda_graph && (!e->ds_on || e->ds_graph_ok))
         {
-            e->launch_forward(true);
+            e->launch_forward(true, greedy);
             CK(cudaStreamSynchronize(e->st));
             e->pull_state_sync();
             e->last += 1;
@@ -1992,7 +2240,7 @@ int ylm_time_decode(ylm_engine *e, int32_t iters, double *ms_per_step)
             NK(ncclAllReduce(e->ar, e->ar, 1, ncclHalf, ncclSum, e->comm, e->st));
         CK(cudaEventRecord(a, e->st));
         for (int i = 0; i < iters; i++)
-            e->launch_forward(true);
+            e->launch_forward(true, greedy);
         CK(cudaEventRecord(b, e->st));
         CK(cudaEventSynchronize(b));
         float ms = 0;

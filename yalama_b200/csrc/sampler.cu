@@ -27,29 +27,6 @@ constexpr int SMP_THREADS = 256;
 constexpr int SMP_KMAX = 64;
 constexpr int SMP_E = 8; // elements per thread in phase 1
 
-__device__ __forceinline__ uint32_t ord16(uint32_t h)
-{
-    return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
-}
-__device__ __forceinline__ uint32_t unord16(uint32_t o) { return (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu); }
-
-__device__ __forceinline__ uint64_t make_key(uint32_t ord, uint32_t idx)
-{
-    return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
-}
-__device__ __forceinline__ uint32_t key_idx(uint64_t k) { return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu); }
-
-__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v)
-{
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-    {
-        uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
-        v = w > v ? w : v;
-    }
-    return v;
-}
-
 // exclusive scan over the block of one int per thread; returns the total in *total
 __device__ __forceinline__ int block_excl_scan(int v, int *wsum, int *total)
 {

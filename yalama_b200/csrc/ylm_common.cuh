@@ -159,6 +159,33 @@ __device__ __forceinline__ float warp_max(float v)
     return v;
 }
 
+// Sampling keys: an FP16 value as a 16-bit unsigned integer with the same
+// order (ord16), and a 64-bit key (ordered value, then the complement of the
+// index) whose maximum is the largest value at its lowest index: argmax's
+// choice among ties.
+__device__ __forceinline__ uint32_t ord16(uint32_t h)
+{
+    return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+__device__ __forceinline__ uint32_t unord16(uint32_t o) { return (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu); }
+
+__device__ __forceinline__ uint64_t make_key(uint32_t ord, uint32_t idx)
+{
+    return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t key_idx(uint64_t k) { return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu); }
+
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+
 // dot of 8 FP16 weights (one 16-byte vector) with 8 FP32 inputs
 __device__ __forceinline__ float dot8(uint4 w, const float *x, float acc)
 {

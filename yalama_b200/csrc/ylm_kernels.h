@@ -155,6 +155,7 @@ struct DsPhase
                           // CTA writes its rows of the embedding row here
     int mbox;             // tensor parallel EPI_RESID: 0 none, 1 / 2 the mailbox set the partial
                           // rows are all-reduced through (see DsArgs::mb)
+    int greedy_pick;      // EPI_STORE of the logits: also pick the argmax (DsArgs::pick_*)
 };
 #define DS_MAX_SEG_PHASES 4
 struct DsArgs
@@ -172,6 +173,13 @@ struct DsArgs
                         // a CTA's rows must not exceed the block size
     unsigned *gen;      // decode steps completed
     int *err;
+    unsigned long long wait_ns; // bound of every wait (YLM_DEV_ERR_TIMEOUT_PEER after it)
+    // greedy sampling fused into the lm_head epilogue (a phase with greedy_pick):
+    // each CTA's best key goes to pick_cand[CTA], the last CTA to finish
+    // (pick_counter, zero between launches) writes the token into pick_state
+    StepState *pick_state;
+    unsigned long long *pick_cand;
+    int *pick_counter;
     // tensor parallelism: rank `rank` of `tp`; mb[s][q] is mailbox set s + 1 of
     // rank q ([tp][hidden] tagged words, slot r written by rank r), mapped
     // into this process (peer memory over NVLink for q != rank)

@@ -89,6 +89,7 @@ class EngineOptions(ctypes.Structure):
         ("zero_kv_on_begin", ctypes.c_int32),
         ("prefill_tensor_cores", ctypes.c_int32),
         ("decode_persistent", ctypes.c_int32),
+        ("wait_limit_us", ctypes.c_int32),
     ]
 
 
@@ -146,6 +147,7 @@ SIGNATURES = {
     "ylm_exchange_stats": (ctypes.c_int, [_P, ctypes.c_int32, _F64P, _F64P, _F64P]),
     "ylm_time_allreduce": (ctypes.c_int, [_P, ctypes.c_int32, _F64P]),
     "ylm_set_attention_path": (ctypes.c_int, [ctypes.c_int32]),
+    "ylm_debug_drop_output": (ctypes.c_int, [_P, ctypes.c_int32]),
     "ylm_k_gemv": (ctypes.c_int, [_P, ctypes.c_int32, ctypes.c_int32, _P, _P, _P]),
     "ylm_k_gemm": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int32, _P]),
     "ylm_k_prefill_attention": (ctypes.c_int, [_P, _P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
@@ -410,6 +412,11 @@ class Engine:
             return None
         check(st, "ylm_time_allreduce")
         return ms.value
+
+    def debug_drop_output(self, layer: int) -> None:
+        """Test support: the persistent path writes `layer`'s SwiGLU activation
+        elsewhere, so the down projection's bounded wait expires (-1 restores)."""
+        check(lib().ylm_debug_drop_output(self._h, layer), "ylm_debug_drop_output")
 
     def decode_persistent(self) -> bool:
         """True when decode steps run as one cooperative kernel."""
