@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 
 // ---------------------------------------------------------------- cluster variant
 // One thread-block cluster per KV head, one CTA per split of the cached
-// tokens (S = cluster size: 8, the portable size, where the device can
-// schedule it; the kernel also supports 16). Inside a CTA each warp takes whole tokens (lane l holds dimensions
+// tokens (S = cluster size: 8, or 16 for launches over 4 KV heads or fewer,
+// where the device schedules them; see attn_cluster_size). Inside a CTA each warp takes whole tokens (lane l holds dimensions
 // 4l..4l+3), ATC_UT tokens per batch: all their scores first, then one
 // rescale of the running softmax state. The 8 warp states are merged in
 // shared memory; each CTA then stores its partial (M, L and one slice of O per
@@ -352,7 +352,7 @@ constexpr int ATC_WARPS = ATC_THREADS / 32;
 constexpr int ATC_MAX_SPLITS = 16; // largest cluster the kernel supports
 constexpr int ATC_MIN_SPLITS = 8;  // smallest cluster (the portable size)
 
-static int g_cluster_splits = 0; // 16, 8, or 0 (no cluster launch: split-K kernel)
+static int g_cluster_splits = 0; // largest schedulable cluster: 16, 8, or 0 (no cluster launch: split-K kernel)
 static int g_force_split = 0;    // 1: the split-K kernel even where clusters launch (tests, diagnostics)
 
 template <int G>
@@ -672,10 +672,7 @@ template <int G> static cudaError_t attn_prepare_t()
 
 cudaError_t attn_prepare()
 {
-    // 8-CTA clusters: at the Llama-3.1-8B shape (8 KV heads, 2-3k cached
-    // tokens) a decode step measured 3.23 ms with 8-CTA clusters against 3.37
-    // with 16 (Qwen3-0.6B: 0.80 against 0.82 ms)
-    int S = 8;
+    int S = 16;
     S = std::min(S, attn_cluster_prepare_t<1>());
     S = std::min(S, attn_cluster_prepare_t<2>());
     S = std::min(S, attn_cluster_prepare_t<3>());
@@ -701,11 +698,23 @@ void attn_force_split_kernel(bool on) { g_force_split = on ? 1 : 0; }
 
 bool attn_uses_split_kernel() { return g_force_split || g_cluster_splits == 0; }
 
+// Cluster size for a launch over `hkv` KV heads: 8 CTAs per head with 8 or
+// more heads (the Llama-3.1-8B shape on one GPU measured 3.23 ms per decode
+// step with 8-CTA clusters against 3.37 with 16; Qwen3-0.6B 0.80 against 0.82),
+// 16 with fewer heads (a tensor-parallel rank's share), so the launch still
+// spreads over more SMs.
+static int attn_cluster_size(int hkv)
+{
+    if (g_force_split || g_cluster_splits == 0)
+        return 0;
+    return hkv <= 4 ? g_cluster_splits : std::min(8, g_cluster_splits);
+}
+
 cudaError_t attn_decode_launch(const AttnArgs &a, cudaStream_t s, bool pdl)
 {
     if (a.hkv <= 0 || a.hq % a.hkv != 0 || a.splits <= 0)
         return cudaErrorInvalidValue;
-    const int S = g_force_split ? 0 : g_cluster_splits;
+    const int S = attn_cluster_size(a.hkv);
     if (S > 0)
         switch (a.hq / a.hkv)
         {

@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // All waits are bounded; a timeout records YLM_DEV_ERR_TIMEOUT_* and unwinds.
 constexpr int FT_BM = 128, FT_BN = 128, FT_THREADS = 320; // TMA, MMA, 8 softmax warps
 constexpr int FT_TILE = 128 * 128 * 2; // one 128 x 128 FP16 tile: two 64-column atoms of 16 KB
-constexpr int FT_TMEM_COLS = 256;
+constexpr int FT_TMEM_COLS = 512; // S for two key tiles (double-buffered), then O
 constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * 6 + 256 + 2 * 2 * 128 * 4; // Q, K x2, V x2, P, barriers, row exchange
 
 // MN-major operand tile with the 128-byte swizzle: 64-element rows along MN,
@@ -393,11 +393,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     uint8_t *sv = sk + 2 * FT_TILE;     // 2 stages
     uint8_t *sp = sv + 2 * FT_TILE;     // P
     uint64_t *bars = reinterpret_cast<uint64_t *>(sp + FT_TILE);
-    uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 6,
-             *o_full = bars + 7, *done = bars + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 10);
-    uint64_t *xbar = bars + 11; // row exchange between the two softmax halves (256 arrivals)
+    uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
+             *o_full = bars + 8, *done = bars + 9;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 11);
+    uint64_t *xbar = bars + 12; // row exchange between the two softmax halves (256 arrivals)
     float *xrow = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256); // maxima [2 halves][128 rows]
     float *xsum = xrow + 256;                                                          // sums [2][128]
 
@@ -414,7 +414,8 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        mbar_init(s_full, 1);
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
         mbar_init(p_full, 256);
         mbar_init(xbar, 256);
         mbar_init(o_full, 1);
@@ -476,34 +477,46 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             const uint32_t idesc_o = tc_idesc(FT_BM, 128) | (1u << 16); // B (V) MN-major
             bool ok = mbar_wait_bounded(q_full, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
             const uint32_t q0 = smem_u32(sq), pb = smem_u32(sp);
-            for (int j = 0; ok && j < nt; j++)
-            {
+            // S_j = Q K_j^T into TMEM columns [128 (j & 1), +128)
+            auto issue_s = [&](int j) {
                 const int s = j & 1;
                 if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
-                {
-                    ok = false;
-                    break;
-                }
+                    return false;
                 tc_fence_after();
-                const uint32_t k0 = smem_u32(sk + s * FT_TILE), v0 = smem_u32(sv + s * FT_TILE);
+                const uint32_t k0 = smem_u32(sk + s * FT_TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++)
                 {
                     const uint32_t off = (uint32_t)((kk >> 2) * (FT_TILE / 2) + (kk & 3) * 32);
-                    tc_mma(tmem, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), idesc_s, kk ? 1u : 0u);
+                    tc_mma(tmem + 128u * s, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), idesc_s, kk ? 1u : 0u);
                 }
-                tc_commit(s_full);
+                tc_commit(&s_full[s]);
+                return true;
+            };
+            ok = ok && issue_s(0);
+            for (int j = 0; ok && j < nt; j++)
+            {
+                const int s = j & 1;
+                // the next tile's scores run on the tensor cores while the
+                // softmax warps work on this one (its S buffer was freed when
+                // tile j - 1's P arrived)
+                if (j + 1 < nt && !issue_s(j + 1))
+                {
+                    ok = false;
+                    break;
+                }
                 if (!mbar_wait_bounded(p_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
                 {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t v0 = smem_u32(sv + s * FT_TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++)
                 {
                     const uint32_t poff = (uint32_t)((kk >> 2) * (FT_TILE / 2) + (kk & 3) * 32);
-                    tc_mma(tmem + 128, smem_desc_k128(pb + poff), smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024),
+                    tc_mma(tmem + 256, smem_desc_k128(pb + poff), smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024),
                            idesc_o, (j | kk) ? 1u : 0u);
                 }
                 tc_commit(o_full);
@@ -532,7 +545,9 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         {
             // (every wait ends in a warp-wide vote: the TMEM accesses below are
             // warp-collective, so the lanes leave together or not at all)
-            const bool sw = mbar_wait_bounded(s_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
+            const bool sw = mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) &&
+                            !*abort_flag;
+            const uint32_t tS = trow + 128u * (uint32_t)(j & 1); // this tile's scores
             if (!__all_sync(0xffffffffu, sw))
             {
                 ok = false;
@@ -546,7 +561,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
-                tmem_ld32(trow + (uint32_t)c0, v);
+                tmem_ld32(tS + (uint32_t)c0, v);
 #pragma unroll
                 for (int i = 0; i < 32; i++)
                     if (key0 + c0 + i <= grow)
@@ -583,11 +598,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     for (int c0 = cb; c0 < cb + 64; c0 += 32)
                     {
                         float v[32];
-                        tmem_ld32(trow + 128u + (uint32_t)c0, v);
+                        tmem_ld32(trow + 256u + (uint32_t)c0, v);
 #pragma unroll
                         for (int i = 0; i < 32; i++)
                             v[i] *= corr;
-                        tmem_st32(trow + 128u + (uint32_t)c0, v);
+                        tmem_st32(trow + 256u + (uint32_t)c0, v);
                     }
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 }
@@ -598,7 +613,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
-                tmem_ld32(trow + (uint32_t)c0, v);
+                tmem_ld32(tS + (uint32_t)c0, v);
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2)
@@ -643,7 +658,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             for (int c0 = cb; c0 < cb + 64; c0 += 32)
             {
                 float v[32];
-                tmem_ld32(trow + 128u + (uint32_t)c0, v);
+                tmem_ld32(trow + 256u + (uint32_t)c0, v);
                 if (grow < p.T)
                 {
 #pragma unroll
