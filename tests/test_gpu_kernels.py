@@ -55,8 +55,10 @@ def test_gemv_matches_fp32(n, k):
 
 
 @pytest.mark.parametrize("tc", [1, 0])
+# the last two have more tiles than SMs: each persistent CTA takes several
+# tiles and reuses both TMEM accumulators (ragged in T, N and K)
 @pytest.mark.parametrize("t,n,k", [(1, 64, 64), (37, 300, 256), (512, 1024, 3072), (128, 5120, 3072),
-                                   (200, 16384, 1024), (129, 257, 136)])
+                                   (200, 16384, 1024), (129, 257, 136), (777, 9000, 320), (1024, 16384, 512)])
 def test_gemm_matches_fp32(t, n, k, tc):
     rng = np.random.default_rng(t + n + k)
     a = rng.standard_normal((t, k)).astype(np.float16)

@@ -26,7 +26,7 @@ constexpr int TC_THREADS = 320; // producer, MMA issuer, 8 epilogue warps
 constexpr int TC_EPI_COLS = TC_BN / 2; // columns per epilogue warp
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2; // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2; // 32 KB
-constexpr int TC_TMEM_COLS = 256;
+constexpr int TC_TMEM_COLS = 512; // two accumulators of TC_BN columns
 constexpr size_t TC_SMEM = 1024 + (size_t)TC_ST * (TC_A_BYTES + TC_B_BYTES) + 256;
 
 struct TcArgs
@@ -105,6 +105,133 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v)
                  : "memory");
 }
 
+// One output tile's epilogue for this thread: TMEM lane quadrant q, columns
+// [cbeg, cbeg + TC_EPI_COLS) of the accumulator at TMEM address tacc.
+__device__ __forceinline__ void tc_epilogue_tile(const TcArgs &p, uint32_t tacc, int m0, int n0, int q, int cbeg,
+                                                 int lane)
+{
+    const int row = m0 + q * 32 + lane;
+    for (int c0 = cbeg; c0 < cbeg + TC_EPI_COLS; c0 += 32)
+    {
+        float v[32];
+        tmem_ld32(tacc + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        const int col0 = n0 + c0;
+        if (row >= p.T || col0 >= p.N)
+            continue;
+        __half *crow = p.C + (int64_t)row * p.ldc;
+        // this thread's 32 columns are 64 contiguous bytes of its row:
+        // 16-byte accesses where the row start keeps them aligned
+        // (a warp's lanes are 32 different rows, so 2-byte accesses
+        // would cost one memory transaction per element)
+        const bool vec = col0 + 32 <= p.N && (p.ldc % 8) == 0;
+        if (p.epi == GEMM_SWIGLU)
+        {
+            __half *dst = crow + (col0 >> 1);
+            if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0)
+            {
+                uint4 pk[2];
+                __half *hh = reinterpret_cast<__half *>(pk);
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                {
+                    const float g = rh(v[2 * j]), u = rh(v[2 * j + 1]);
+                    const float sg = rh(g / (1.0f + expf(-g)));
+                    hh[j] = f2h(sg * u);
+                }
+                reinterpret_cast<uint4 *>(dst)[0] = pk[0];
+                reinterpret_cast<uint4 *>(dst)[1] = pk[1];
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                {
+                    const int col = col0 + j;
+                    if (col < p.N)
+                    {
+                        const float g = rh(v[j]), u = rh(v[j + 1]);
+                        const float sg = rh(g / (1.0f + expf(-g)));
+                        crow[col >> 1] = f2h(sg * u);
+                    }
+                }
+            }
+        }
+        else if (p.epi == GEMM_RESID)
+        {
+            if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0)
+            {
+                uint4 *rp = reinterpret_cast<uint4 *>(crow + col0);
+                uint4 r[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    r[j] = rp[j];
+                __half *rr = reinterpret_cast<__half *>(r);
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    rr[j] = f2h(h2f(rr[j]) + rh(v[j]));
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    rp[j] = r[j];
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if (col0 + j < p.N)
+                        crow[col0 + j] = f2h(h2f(crow[col0 + j]) + rh(v[j]));
+            }
+        }
+        else
+        {
+            if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0 &&
+                (!p.bias || (reinterpret_cast<uintptr_t>(p.bias + col0) & 15) == 0))
+            {
+                uint4 pk[4];
+                __half *hh = reinterpret_cast<__half *>(pk);
+                if (p.bias)
+                {
+                    uint4 bq[4];
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        bq[j] = reinterpret_cast<const uint4 *>(p.bias + col0)[j];
+                    const __half *bb = reinterpret_cast<const __half *>(bq);
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        hh[j] = f2h(rh(v[j]) + h2f(bb[j]));
+                }
+                else
+                {
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        hh[j] = f2h(v[j]);
+                }
+                uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    dst[j] = pk[j];
+            }
+            else
+            {
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if (col0 + j < p.N)
+                    {
+                        float y = v[j];
+                        if (p.bias)
+                            y = rh(y) + h2f(p.bias[col0 + j]);
+                        crow[col0 + j] = f2h(y);
+                    }
+            }
+        }
+    }
+}
+
+// Persistent: one CTA per SM walks the output tiles blockIdx.x, + gridDim.x,
+// ... (M-fastest order: the CTAs of a wave that share a W tile run together,
+// so each W tile comes from HBM once and A stays in L2). The producer's ring
+// of operand stages runs on across tiles; the accumulator is double-buffered in
+// TMEM (2 x 256 columns), so the epilogue warps drain tile i while the MMA
+// warp accumulates tile i + 1.
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap, const TcArgs p)
 {
@@ -114,16 +241,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t *sb = smem + (size_t)TC_ST * TC_A_BYTES;
     uint64_t *full = reinterpret_cast<uint64_t *>(sb + (size_t)TC_ST * TC_B_BYTES);
     uint64_t *empty = full + TC_ST;
-    uint64_t *accum = empty + TC_ST;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
-    int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+    uint64_t *acc_full = empty + TC_ST; // [2] MMA -> epilogue
+    uint64_t *acc_empty = acc_full + 2; // [2] epilogue (8 warps) -> MMA
+    uint64_t *done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // tiles in M-fastest order: the CTAs of a wave that share a W tile run
-    // together, so each W tile comes from HBM once and A stays in L2 (with N
-    // fastest, a W larger than L2 was re-read once per 128-row block)
     const int mt = (p.T + TC_BM - 1) / TC_BM;
-    const int n0 = (int)(blockIdx.x / mt) * TC_BN, m0 = (int)(blockIdx.x % mt) * TC_BM;
+    const int tiles = mt * ((p.N + TC_BN - 1) / TC_BN);
     const int KT = (p.K + TC_BK - 1) / TC_BK;
 
     if (threadIdx.x == 0)
@@ -133,7 +259,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int b = 0; b < 2; b++)
+        {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], TC_THREADS / 32 - 2);
+        }
+        mbar_init(done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -155,22 +286,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         {
             prefetch_tensormap(&amap);
             prefetch_tensormap(&wmap);
-            int issued = 0;
-            for (int kt = 0; kt < KT; kt++)
+            int g = 0; // k-stages issued by this CTA, over all its tiles
+            for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x)
             {
-                const int s = kt % TC_ST;
-                if (kt >= TC_ST && !mbar_wait_bounded(&empty[s], ((kt / TC_ST) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                const int n0 = (t / mt) * TC_BN, m0 = (t % mt) * TC_BM;
+                for (int kt = 0; kt < KT; kt++, g++)
                 {
-                    *abort_flag = 1;
-                    break;
+                    const int s = g % TC_ST;
+                    if (g >= TC_ST &&
+                        !mbar_wait_bounded(&empty[s], ((g / TC_ST) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                    {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], TC_A_BYTES + TC_B_BYTES);
+                    tma_load_2d(sa + (size_t)s * TC_A_BYTES, &amap, kt * TC_BK, m0, &full[s]);
+                    tma_load_2d(sb + (size_t)s * TC_B_BYTES, &wmap, kt * TC_BK, n0, &full[s]);
                 }
-                mbar_arrive_expect_tx(&full[s], TC_A_BYTES + TC_B_BYTES);
-                tma_load_2d(sa + (size_t)s * TC_A_BYTES, &amap, kt * TC_BK, m0, &full[s]);
-                tma_load_2d(sb + (size_t)s * TC_B_BYTES, &wmap, kt * TC_BK, n0, &full[s]);
-                issued++;
             }
-            for (int kt = issued > TC_ST ? issued - TC_ST : 0; kt < issued; kt++)
-                mbar_wait_bounded(&full[kt % TC_ST], (kt / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+            // every issued copy has landed before the CTA can exit
+            for (int h = g > TC_ST ? g - TC_ST : 0; h < g; h++)
+                mbar_wait_bounded(&full[h % TC_ST], (h / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
         }
     }
     else if (warp == 1)
@@ -178,151 +314,73 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0)
         {
             const uint32_t idesc = tc_idesc(TC_BM, TC_BN);
-            for (int kt = 0; kt < KT; kt++)
+            int g = 0;
+            bool ok = true;
+            int i = 0; // this CTA's tile count
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, i++)
             {
-                const int s = kt % TC_ST;
-                if (!mbar_wait_bounded(&full[s], (kt / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                const int b = i & 1;
+                const uint32_t tacc = tmem + (uint32_t)(b * TC_BN);
+                // the epilogue has drained this accumulator's previous tile
+                if (i >= 2 && !mbar_wait_bounded(&acc_empty[b], ((i >> 1) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
                 {
-                    *abort_flag = 1;
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sa + (size_t)s * TC_A_BYTES);
-                const uint32_t b0 = smem_u32(sb + (size_t)s * TC_B_BYTES);
+                for (int kt = 0; kt < KT; kt++, g++)
+                {
+                    const int s = g % TC_ST;
+                    if (!mbar_wait_bounded(&full[s], (g / TC_ST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                    {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sa + (size_t)s * TC_A_BYTES);
+                    const uint32_t b0 = smem_u32(sb + (size_t)s * TC_B_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < TC_BK / 16; kk++)
-                    tc_mma(tmem, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
-                           (kt | kk) != 0 ? 1u : 0u);
-                tc_commit(&empty[s]); // stage free once these MMAs have read it
+                    for (int kk = 0; kk < TC_BK / 16; kk++)
+                        tc_mma(tacc, smem_desc_k128(a0 + kk * 32), smem_desc_k128(b0 + kk * 32), idesc,
+                               (kt | kk) != 0 ? 1u : 0u);
+                    tc_commit(&empty[s]); // stage free once these MMAs have read it
+                }
+                if (ok)
+                    tc_commit(&acc_full[b]); // this tile's MMAs complete -> epilogue
             }
-            tc_commit(accum); // all issued MMAs complete -> epilogue
+            if (!ok)
+                *abort_flag = 1;
+            // all issued MMAs complete before TMEM is released
+            tc_commit(done);
+            mbar_wait_bounded(done, 0, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
         }
         __syncwarp();
     }
     else
     {
         // epilogue warps 2..9 -> TMEM lane quadrant (warp % 4); warps 2-5 take
-        // columns [0, 128), warps 6-9 columns [128, 256)
+        // columns [0, 128), warps 6-9 columns [128, 256) of each tile
         const int q = warp & 3;
         const int cbeg = ((warp - 2) >> 2) * TC_EPI_COLS;
-        const int row = m0 + q * 32 + lane;
-        const bool ok = mbar_wait_bounded(accum, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
-        tc_fence_after();
-        if (ok && !*abort_flag)
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++)
         {
-            for (int c0 = cbeg; c0 < cbeg + TC_EPI_COLS; c0 += 32)
+            const int b = i & 1;
+            // (a warp-wide vote: the TMEM loads below are warp-collective)
+            const bool ok = mbar_wait_bounded(&acc_full[b], (i >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) &&
+                            !*abort_flag;
+            if (!__all_sync(0xffffffffu, ok))
             {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-                const int col0 = n0 + c0;
-                if (row >= p.T || col0 >= p.N)
-                    continue;
-                __half *crow = p.C + (int64_t)row * p.ldc;
-                // this thread's 32 columns are 64 contiguous bytes of its row:
-                // 16-byte accesses where the row start keeps them aligned
-                // (a warp's lanes are 32 different rows, so 2-byte accesses
-                // would cost one memory transaction per element)
-                const bool vec = col0 + 32 <= p.N && (p.ldc % 8) == 0;
-                if (p.epi == GEMM_SWIGLU)
-                {
-                    __half *dst = crow + (col0 >> 1);
-                    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0)
-                    {
-                        uint4 pk[2];
-                        __half *hh = reinterpret_cast<__half *>(pk);
-#pragma unroll
-                        for (int j = 0; j < 16; j++)
-                        {
-                            const float g = rh(v[2 * j]), u = rh(v[2 * j + 1]);
-                            const float sg = rh(g / (1.0f + expf(-g)));
-                            hh[j] = f2h(sg * u);
-                        }
-                        reinterpret_cast<uint4 *>(dst)[0] = pk[0];
-                        reinterpret_cast<uint4 *>(dst)[1] = pk[1];
-                    }
-                    else
-                    {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 2)
-                        {
-                            const int col = col0 + j;
-                            if (col < p.N)
-                            {
-                                const float g = rh(v[j]), u = rh(v[j + 1]);
-                                const float sg = rh(g / (1.0f + expf(-g)));
-                                crow[col >> 1] = f2h(sg * u);
-                            }
-                        }
-                    }
-                }
-                else if (p.epi == GEMM_RESID)
-                {
-                    if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0)
-                    {
-                        uint4 *rp = reinterpret_cast<uint4 *>(crow + col0);
-                        uint4 r[4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            r[j] = rp[j];
-                        __half *rr = reinterpret_cast<__half *>(r);
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            rr[j] = f2h(h2f(rr[j]) + rh(v[j]));
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            rp[j] = r[j];
-                    }
-                    else
-                    {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (col0 + j < p.N)
-                                crow[col0 + j] = f2h(h2f(crow[col0 + j]) + rh(v[j]));
-                    }
-                }
-                else
-                {
-                    if (vec && (reinterpret_cast<uintptr_t>(crow + col0) & 15) == 0 &&
-                        (!p.bias || (reinterpret_cast<uintptr_t>(p.bias + col0) & 15) == 0))
-                    {
-                        uint4 pk[4];
-                        __half *hh = reinterpret_cast<__half *>(pk);
-                        if (p.bias)
-                        {
-                            uint4 bq[4];
-#pragma unroll
-                            for (int j = 0; j < 4; j++)
-                                bq[j] = reinterpret_cast<const uint4 *>(p.bias + col0)[j];
-                            const __half *bb = reinterpret_cast<const __half *>(bq);
-#pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                hh[j] = f2h(rh(v[j]) + h2f(bb[j]));
-                        }
-                        else
-                        {
-#pragma unroll
-                            for (int j = 0; j < 32; j++)
-                                hh[j] = f2h(v[j]);
-                        }
-                        uint4 *dst = reinterpret_cast<uint4 *>(crow + col0);
-#pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            dst[j] = pk[j];
-                    }
-                    else
-                    {
-#pragma unroll
-                        for (int j = 0; j < 32; j++)
-                            if (col0 + j < p.N)
-                            {
-                                float y = v[j];
-                                if (p.bias)
-                                    y = rh(y) + h2f(p.bias[col0 + j]);
-                                crow[col0 + j] = f2h(y);
-                            }
-                    }
-                }
+                *abort_flag = 1;
+                break;
             }
+            tc_fence_after();
+            tc_epilogue_tile(p, tmem + (uint32_t)(b * TC_BN), (t % mt) * TC_BM, (t / mt) * TC_BN, q, cbeg, lane);
+            // this warp's reads of the accumulator are done: it may be reused
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&acc_empty[b]);
         }
     }
     tc_fence_before();
@@ -381,6 +439,15 @@ struct FtArgs
     __half *out; // [T][hq * 128]
     int *err;
 };
+
+// 2^x with the PTX ex2.approx instruction, subnormal results flushed to zero:
+// the softmax's arguments are <= 0, and values below 2^-126 vanish in FP16 P.
+__device__ __forceinline__ float ex2_ftz(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __global__ void __launch_bounds__(FT_THREADS, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -555,17 +622,31 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             }
             tc_fence_after();
             const int key0 = j * FT_BN;
+            // only the diagonal tile holds keys past some of its rows
+            const bool diag = j == nt - 1;
+            // this thread's 64 scores, read from TMEM once, scaled to base 2;
             // pass 1: the row maximum of this tile (masked keys excluded)
+            float v[64];
+            tmem_ld32(tS + (uint32_t)cb, v);
+            tmem_ld32(tS + (uint32_t)cb + 32u, v + 32);
             float mx = -INFINITY;
-#pragma unroll
-            for (int c0 = cb; c0 < cb + 64; c0 += 32)
+            if (diag)
             {
-                float v[32];
-                tmem_ld32(tS + (uint32_t)c0, v);
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    if (key0 + c0 + i <= grow)
-                        mx = fmaxf(mx, v[i] * sl2);
+                for (int i = 0; i < 64; i++)
+                {
+                    v[i] = key0 + cb + i <= grow ? v[i] * sl2 : -INFINITY;
+                    mx = fmaxf(mx, v[i]);
+                }
+            }
+            else
+            {
+#pragma unroll
+                for (int i = 0; i < 64; i++)
+                {
+                    v[i] *= sl2;
+                    mx = fmaxf(mx, v[i]);
+                }
             }
             // the row's other half, through shared memory (a thread writes the
             // next tile's value only after both halves arrived on p_full for
@@ -608,18 +689,17 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 }
             }
             // pass 2: P = exp2(s - m) in FP16, 16-byte chunks into the swizzled layout
+            // (masked keys hold -inf: exp2 gives 0)
             float sum = 0.f;
 #pragma unroll
-            for (int c0 = cb; c0 < cb + 64; c0 += 32)
+            for (int c0 = 0; c0 < 64; c0 += 32)
             {
-                float v[32];
-                tmem_ld32(tS + (uint32_t)c0, v);
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2)
                 {
-                    const float p0 = key0 + c0 + i <= grow ? exp2f(v[i] * sl2 - mn) : 0.f;
-                    const float p1 = key0 + c0 + i + 1 <= grow ? exp2f(v[i + 1] * sl2 - mn) : 0.f;
+                    const float p0 = ex2_ftz(v[c0 + i] - mn);
+                    const float p1 = ex2_ftz(v[c0 + i + 1] - mn);
                     sum += p0 + p1;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&hp);
@@ -627,7 +707,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
 #pragma unroll
                 for (int ch = 0; ch < 4; ch++)
                 {
-                    const int c = (c0 >> 3) + ch; // 16-byte chunk of the row: keys 8c .. 8c + 7
+                    const int c = ((cb + c0) >> 3) + ch; // 16-byte chunk of the row: keys 8c .. 8c + 7
                     uint8_t *dst = sp + (c >> 3) * (FT_TILE / 2) + row * 128 + (((c & 7) ^ (row & 7)) << 4);
                     *reinterpret_cast<uint4 *>(dst) =
                         make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
@@ -745,7 +825,18 @@ cudaError_t gemm_tc_launch(const CUtensorMap &amap, const CUtensorMap &wmap, int
     a.C = C;
     a.ldc = ldc;
     a.err = err;
-    dim3 grid((unsigned)(((N + TC_BN - 1) / TC_BN) * ((T + TC_BM - 1) / TC_BM)));
+    // persistent: at most one CTA per SM, each walking its share of the tiles
+    static int sms = 0;
+    if (!sms)
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0)
+            sms = 148;
+    }
+    const int tiles = ((N + TC_BN - 1) / TC_BN) * ((T + TC_BM - 1) / TC_BM);
+    dim3 grid((unsigned)std::min(tiles, sms));
     gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(amap, wmap, a);
     return cudaGetLastError();
 }

@@ -59,8 +59,68 @@ cudaError_t resid_add_rows_launch(__half *x, const __half *y, int64_t n, cudaStr
 }
 
 // ------------------------------------------------------------------ RMSNorm rows
-// ModelBase.cpp:724-736 with FP16 rounding after each op.
-__global__ void rmsnorm_rows_kernel(const __half *x, const __half *w, float eps, int H, __half *y)
+// ModelBase.cpp:724-736 with FP16 rounding after each op. One CTA per row;
+// each thread holds its 16-byte chunks of the row in registers, so the row is
+// read from memory once (RN_CHUNKS x 8 halves x RN_THREADS covers H <= 8192).
+constexpr int RN_THREADS = 128, RN_CHUNKS = 8;
+
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const __half *x, const __half *w, float eps, int H,
+                                                                 __half *y)
+{
+    __shared__ float red[RN_THREADS / 32];
+    const int t = blockIdx.x, nv = H >> 3;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (int64_t)t * H);
+    uint4 v[RN_CHUNKS];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < RN_CHUNKS; c++)
+    {
+        const int i = threadIdx.x + c * RN_THREADS;
+        if (i < nv)
+        {
+            v[c] = xr[i];
+            const __half *h = reinterpret_cast<const __half *>(&v[c]);
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+            {
+                const float f = h2f(h[e]);
+                ss += rh(f * f);
+            }
+        }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < RN_THREADS / 32; i++)
+        tot += red[i];
+    const float mean = rh(tot * (1.0f / (float)H));
+    const float d = rh(rsqrtf(mean + eps));
+    const uint4 *wr = reinterpret_cast<const uint4 *>(w);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + (int64_t)t * H);
+#pragma unroll
+    for (int c = 0; c < RN_CHUNKS; c++)
+    {
+        const int i = threadIdx.x + c * RN_THREADS;
+        if (i < nv)
+        {
+            const uint4 wv = wr[i];
+            const __half *h = reinterpret_cast<const __half *>(&v[c]);
+            const __half *wh = reinterpret_cast<const __half *>(&wv);
+            uint4 o;
+            __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                oh[e] = f2h(rh(h2f(h[e]) * d) * h2f(wh[e]));
+            yr[i] = o;
+        }
+    }
+}
+
+// Rows whose width is not a multiple of 8 halves or above the register budget.
+__global__ void rmsnorm_rows_scalar_kernel(const __half *x, const __half *w, float eps, int H, __half *y)
 {
     __shared__ float red[32];
     const int t = blockIdx.x;
@@ -88,7 +148,12 @@ cudaError_t rmsnorm_rows_launch(const __half *x, const __half *w, float eps, int
 {
     if (T <= 0)
         return cudaSuccess;
-    rmsnorm_rows_kernel<<<T, 256, 0, s>>>(x, w, eps, H, y);
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                           reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (aligned && H % 8 == 0 && H <= 8 * RN_THREADS * RN_CHUNKS)
+        rmsnorm_rows_kernel<<<T, RN_THREADS, 0, s>>>(x, w, eps, H, y);
+    else
+        rmsnorm_rows_scalar_kernel<<<T, 256, 0, s>>>(x, w, eps, H, y);
     return cudaGetLastError();
 }
 
@@ -182,10 +247,25 @@ cudaError_t gemm_launch(const __half *A, int lda, const __half *W, int T, int N,
 }
 
 // ------------------------------------------------------------------ q/k-norm, RoPE, KV write
-// grid (T, hq + 2*hkv), one warp per (token, head). Positions pos0 + t.
-__global__ void qkv_post_prefill_kernel(const QkvPostArgs a)
+// grid (T, ceil((hq + 2*hkv) / QP_WARPS)), one warp per (token, head); lane l
+// holds head dims 4l..4l+3 (8-byte loads and stores). Positions pos0 + t.
+constexpr int QP_WARPS = 4;
+
+__device__ __forceinline__ void ld4h(const __half *p, float x[4])
 {
-    const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const __half *h = reinterpret_cast<const __half *>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+        x[e] = h2f(h[e]);
+}
+
+__global__ void __launch_bounds__(QP_WARPS * 32) qkv_post_prefill_kernel(const QkvPostArgs a)
+{
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x, h = blockIdx.y * QP_WARPS + (threadIdx.x >> 5);
+    if (h >= a.hq + 2 * a.hkv)
+        return;
     const int width = (a.hq + 2 * a.hkv) * YLM_HEAD_DIM;
     const __half *src = a.qkv + (int64_t)t * width + (int64_t)h * YLM_HEAD_DIM;
     const int pos = a.pos0 + t;
@@ -193,45 +273,54 @@ __global__ void qkv_post_prefill_kernel(const QkvPostArgs a)
     {
         const int g = h - a.hq - a.hkv;
         __half *dst = a.v_cache + ((int64_t)g * a.cap + pos) * YLM_HEAD_DIM;
-        for (int d = lane; d < YLM_HEAD_DIM; d += 32)
-            dst[d] = src[d];
+        reinterpret_cast<uint2 *>(dst)[lane] = reinterpret_cast<const uint2 *>(src)[lane];
         return;
     }
     const bool is_q = h < a.hq;
     float x[4];
-    for (int e = 0; e < 4; e++)
-        x[e] = h2f(src[lane * 4 + e]);
+    ld4h(src + lane * 4, x);
     const __half *nw = is_q ? a.q_norm : a.k_norm;
     if (nw)
     {
         float ss = 0.f;
+#pragma unroll
         for (int e = 0; e < 4; e++)
             ss += rh(x[e] * x[e]);
         ss = warp_sum(ss);
         const float mean = rh(ss * (1.0f / YLM_HEAD_DIM));
         const float dn = rh(rsqrtf(mean + a.eps));
+        float wv[4];
+        ld4h(nw + lane * 4, wv);
+#pragma unroll
         for (int e = 0; e < 4; e++)
-            x[e] = rh(rh(x[e] * dn) * h2f(nw[lane * 4 + e]));
+            x[e] = rh(rh(x[e] * dn) * wv[e]);
     }
     float px[4];
+#pragma unroll
     for (int e = 0; e < 4; e++)
         px[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-    const __half *cr = a.rope_cos + (int64_t)pos * 64, *sr = a.rope_sin + (int64_t)pos * 64;
+    float cv[4], sv[4];
+    ld4h(a.rope_cos + (int64_t)pos * 64 + (lane & 15) * 4, cv);
+    ld4h(a.rope_sin + (int64_t)pos * 64 + (lane & 15) * 4, sv);
     __half *dst = is_q ? a.q_out + (int64_t)t * a.hq * YLM_HEAD_DIM + (int64_t)h * YLM_HEAD_DIM
                        : a.k_cache + ((int64_t)(h - a.hq) * a.cap + pos) * YLM_HEAD_DIM;
+    uint2 o;
+    __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
     for (int e = 0; e < 4; e++)
     {
-        const int d = lane * 4 + e;
-        const float rot = d < 64 ? -px[e] : px[e];
-        dst[d] = f2h(rh(rh(x[e] * h2f(cr[d & 63])) + rh(rot * h2f(sr[d & 63]))));
+        const float rot = lane < 16 ? -px[e] : px[e];
+        oh[e] = f2h(rh(rh(x[e] * cv[e]) + rh(rot * sv[e])));
     }
+    reinterpret_cast<uint2 *>(dst)[lane] = o;
 }
 
 cudaError_t qkv_post_prefill_launch(const QkvPostArgs &a, cudaStream_t s)
 {
     if (a.T <= 0)
         return cudaSuccess;
-    qkv_post_prefill_kernel<<<dim3(a.T, a.hq + 2 * a.hkv), 32, 0, s>>>(a);
+    const int heads = a.hq + 2 * a.hkv;
+    qkv_post_prefill_kernel<<<dim3(a.T, (heads + QP_WARPS - 1) / QP_WARPS), QP_WARPS * 32, 0, s>>>(a);
     return cudaGetLastError();
 }
 
