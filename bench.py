@@ -325,6 +325,34 @@ def gpu_reference(spec, prompt, top_k, temp):
     return out
 
 
+# ---------------------------------------------------------------- host BPE encode
+TOKENIZER_BENCH = os.path.join(ROOT, "yalama_b200", "host", "_build", "tokenizer_bench")
+
+
+def host_bpe_encode(n_bytes=32000, n_merges=50000):
+    """The prompt-encoding step before the token loop: a 32 KB Qwen-family
+    prompt (one BPE piece) with a 50k-merge synthetic tokenizer, encoded by the
+    reference's QwenTokenizer and by its FastBpe wrapper (ids compared), median
+    wall time of each on one host core."""
+    if not os.path.exists(TOKENIZER_BENCH):
+        return {"value": None, "error": "tokenizer_bench not built (it needs the reference sources at build time)"}
+    from yalama_b200 import synth
+    with tempfile.TemporaryDirectory() as tmp:
+        synth.write_bpe_tokenizer(tmp, "qwen", n_merges, seed=0)
+        tp = os.path.join(tmp, "prompt.txt")
+        with open(tp, "w", encoding="utf-8") as f:
+            f.write(synth.bpe_text("qwen", n_bytes, seed=0))
+        r = subprocess.run([TOKENIZER_BENCH, "--model", tmp, "--family", "qwen", "--text", tp, "--reps", "5",
+                            "--ref-reps", "1"], capture_output=True, text=True, timeout=300)
+    if r.returncode != 0:
+        return {"value": None, "error": r.stderr[-300:]}
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    return {"value": res["fast_ms"], "unit": "ms", "reference_ms": res["ref_ms"], "tokens": res["tokens"],
+            "ids_equal_reference": res["equal"],
+            "sample": f"{res['bytes']}-byte synthetic prompt, {n_merges}-merge byte-level BPE, Qwen family "
+                      "(whole text one piece), EncodeWithoutChatTemplate, BPE cache cleared per run"}
+
+
 # ---------------------------------------------------------------- our engine
 def segment_roofline(eng, spec, hbm_peak, peak_kind):
     """The dominant kernel of the persistent path: one decode GEMV segment (a
@@ -527,6 +555,8 @@ def bench_ours(a):
                                     "kind": kind, "sample": sample}
         except Exception as ex:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(ex)[:300]}
+    if world == 1 and not a.layers:
+        line["host_bpe_encode"] = host_bpe_encode()
     if world == 1 and not a.no_ref_gpu and not a.layers:
         from yalama_b200 import synth as sy
         try:

@@ -468,3 +468,125 @@ def write_tokenizer(snap: str, spec: ModelSpec, family: str = "llama", n_merges:
     with open(cfg_path, "w") as f:
         json.dump(cfg, f, indent=1)
     return sp
+
+
+# ---------------------------------------------------------------- large BPE tokenizers
+# A tokenizer.json with tens of thousands of merges and a text to encode with
+# it, for checking and timing the host BPE encoder on long prompts. The merge
+# table is built from a seeded lexicon of syllable words (pairwise, level by
+# level, most frequent words first), so merges nest the way trained ones do;
+# the text draws those words with Zipf frequencies, with punctuation, digits,
+# newlines and multi-byte characters, and optional special tokens.
+_SYL_CONS = ["b", "c", "d", "f", "g", "h", "j", "k", "l", "m", "n", "p", "r", "s", "t", "v", "w", "z",
+             "ch", "sh", "th", "st", "tr", "pl"]
+_SYL_VOWS = ["a", "e", "i", "o", "u", "ai", "ea", "ou", "é", "ü", "ø"]
+
+
+def _lexicon(rng: np.random.Generator, n_words: int) -> List[str]:
+    seen, out = set(), []
+    while len(out) < n_words:
+        k = int(rng.integers(1, 5))
+        w = ""
+        for _ in range(k):
+            w += _SYL_CONS[int(rng.integers(len(_SYL_CONS)))] + _SYL_VOWS[int(rng.integers(len(_SYL_VOWS)))]
+            if rng.random() < 0.3:
+                w += _SYL_CONS[int(rng.integers(len(_SYL_CONS)))]
+        if rng.random() < 0.02:
+            w += "中"  # a 3-byte character
+        if w not in seen:
+            seen.add(w)
+            out.append(w)
+    return out
+
+
+def _symbols(text: str, family: str) -> List[str]:
+    """The base symbols the reference's tokenizer splits `text` into before BPE:
+    byte-alphabet characters (Llama, Qwen) or UTF-8 characters with '▁' for
+    a space (Mistral)."""
+    if family == "mistral":
+        return list(text.replace(" ", "▁"))
+    alpha = byte_alphabet()
+    return [alpha[b] for b in text.encode()]
+
+
+def bpe_tokenizer(family: str, n_merges: int, seed: int = 0, n_words: int = 20000):
+    """(vocab {token: id}, merges ["a b"], special {token: id}, lexicon)."""
+    rng = np.random.default_rng(seed)
+    lex = _lexicon(rng, n_words)
+    if family == "mistral":
+        base = sorted(set("".join(lex)) | set(" ,.?!:;'\n0123456789-") - {" "}) + ["▁"]
+        vocab: Dict[str, int] = {"<unk>": 0}
+        for c in base:
+            vocab.setdefault(c, len(vocab))
+    else:
+        vocab = {c: i for i, c in enumerate(byte_alphabet())}
+    merges: List[str] = []
+    have = set()
+    for w in lex:
+        for form in (" " + w, w):
+            s = _symbols(form, family)
+            while len(s) > 1 and len(merges) < n_merges:
+                nxt = []
+                for i in range(0, len(s), 2):
+                    if i + 1 < len(s):
+                        key = s[i] + " " + s[i + 1]
+                        if key not in have:
+                            have.add(key)
+                            merges.append(key)
+                            vocab.setdefault(s[i] + s[i + 1], len(vocab))
+                        nxt.append(s[i] + s[i + 1])
+                    else:
+                        nxt.append(s[i])
+                s = nxt
+        if len(merges) >= n_merges:
+            break
+    specials = SPECIAL_TOKENS["qwen" if family == "qwen" else "llama"]
+    sp = {t: len(vocab) + i for i, t in enumerate(specials)}
+    return vocab, merges, sp, lex
+
+
+def write_bpe_tokenizer(folder: str, family: str, n_merges: int, seed: int = 0) -> Dict[str, int]:
+    """Write `folder`/tokenizer.json (the layout LoadFromJson reads,
+    src/tokenizer/TokenizerBase.cpp:65-208). Returns the special tokens' ids."""
+    vocab, merges, sp, _ = bpe_tokenizer(family, n_merges, seed)
+    tok = {
+        "version": "1.0",
+        "added_tokens": [{"id": i, "content": t, "single_word": False, "lstrip": False, "rstrip": False,
+                          "normalized": False, "special": True} for t, i in sp.items()],
+        "model": {"type": "BPE", "vocab": vocab, "merges": merges},
+    }
+    os.makedirs(folder, exist_ok=True)
+    with open(os.path.join(folder, "tokenizer.json"), "w", encoding="utf-8") as f:
+        json.dump(tok, f, ensure_ascii=False)
+    return sp
+
+
+def bpe_text(family: str, n_bytes: int, seed: int = 0, specials_every: int = 0, n_merges: int = 0) -> str:
+    """About `n_bytes` of text in the lexicon of bpe_tokenizer(family, seed);
+    a special token of the family after every `specials_every` words (0: none)."""
+    rng = np.random.default_rng(seed + 1)
+    lex = _lexicon(np.random.default_rng(seed), 20000)
+    p = 1.0 / (np.arange(len(lex)) + 10.0)
+    p /= p.sum()
+    specials = SPECIAL_TOKENS["qwen" if family == "qwen" else "llama"]
+    out, size, nw = [], 0, 0
+    picks, rolls, k = np.empty(0, np.int64), np.empty(0), 0
+    while size < n_bytes:
+        if k == len(picks):
+            picks, rolls, k = rng.choice(len(lex), size=4096, p=p), rng.random(4096), 0
+        w, r = lex[int(picks[k])], float(rolls[k])
+        k += 1
+        if r < 0.05:
+            w += ","
+        elif r < 0.08:
+            w += "."
+        elif r < 0.09:
+            w += "?\n"
+        elif r < 0.10:
+            w = str(int(rng.integers(0, 100000)))
+        out.append(w)
+        size += len(w.encode()) + 1
+        nw += 1
+        if specials_every and nw % specials_every == 0:
+            out.append(specials[int(rng.integers(len(specials)))])
+    return " ".join(out)
