@@ -347,6 +347,17 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const AttnArgs
 // head) into the shared memory of the rank that owns that slice (distributed
 // shared memory), and after one cluster barrier every rank combines its slice
 // of the S partials and writes it. No global scratch, fence or atomic ticket.
+// D (rows 0..7 of a 16 x 8 FP32 tile, d0 d1) += A B with A rows 8..15 zero:
+// mma.sync m16n8k16, FP16 operands (a0 = A[r][2q..], a2 = A[r][2q+8..]),
+// z0 z1 the unused rows 8..15 of D (they stay zero).
+__device__ __forceinline__ void atm_mma(float &d0, float &d1, float &z0, float &z1, uint32_t a0, uint32_t a2,
+                                        uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d0), "+f"(d1), "+f"(z0), "+f"(z1)
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
 constexpr int ATC_THREADS = 256;
 constexpr int ATC_WARPS = ATC_THREADS / 32;
 constexpr int ATC_MAX_SPLITS = 16; // largest cluster the kernel supports
@@ -358,7 +369,6 @@ static int g_force_split = 0;    // 1: the split-K kernel even where clusters la
 template <int G>
 __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArgs a)
 {
-    constexpr int UT = G <= 4 ? 8 : 4; // tokens per warp batch
     __shared__ float q_s[G * YLM_HEAD_DIM];
     __shared__ float kn_s[YLM_HEAD_DIM], vn_s[YLM_HEAD_DIM];
     __shared__ float mrg[ATC_WARPS * G * ATT_ROW];
@@ -384,25 +394,57 @@ __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArg
     const int t0 = min(n, sp * chunk), t1 = min(n, t0 + chunk);
     const bool owns_new = ok && slot >= t0 && slot < t1;
     const int te = owns_new ? slot : t1; // cached tokens [t0, te); the new one comes from qkv
-    const __half *kc = a.k_cache + (size_t)g * a.cap * YLM_HEAD_DIM + lane * 4;
-    const __half *vc = a.v_cache + (size_t)g * a.cap * YLM_HEAD_DIM + lane * 4;
 
-    // token j of this warp: t0 + warp + 8 j; earlier slots are constant during
-    // the step, so the first batch is loaded before griddepcontrol.wait
-    uint2 kr[UT], vr[UT];
-    auto load_batch = [&](int j0) {
+    // Cached tokens [t0, te) in chunks of 16, chunk c = tokens t0 + 16 c ...,
+    // warp w taking chunks w, w + 8, ...; both products of a chunk on the
+    // tensor cores (mma.sync m16n8k16, FP16 inputs, FP32 accumulation), the G
+    // query heads of the group as rows 0..G-1 of M (rows G..15 zero).
+    // Lane l works on head row m = l / 4 and quarter kq = l % 4.
+    //  S = Q K^T: the head dimension is summed in a permuted order so that
+    //    every B fragment comes from 16-byte loads of K rows: in k-step
+    //    j = 2 s + t, k positions 2 kq + {0, 1} and 2 kq + 8 + {0, 1} are
+    //    dimensions 32 kq + 8 s + 4 t + {0, 1} and + {2, 3}; n position p of
+    //    n-tile b is token 8 b + p of the chunk. Lane l loads dimensions
+    //    [32 kq, 32 kq + 32) of tokens l / 4 and 8 + l / 4.
+    //  O += P V: k = the chunk's 16 tokens (P straight from the S
+    //    accumulators), n-tile i position p = dimension 16 p + i, so lane l
+    //    loads dimensions [16 (l / 4), + 16) of tokens 2 kq + {0, 1, 8, 9},
+    //    and its O accumulators are head m, dimensions 32 kq + 16 c + i.
+    // Earlier slots are constant during the step: each warp's first chunk is
+    // loaded before griddepcontrol.wait.
+    const int nchunks = (te - t0 + 15) >> 4;
+    const int hm = lane >> 2, kq = lane & 3;
+    const __half *kc = a.k_cache + (size_t)g * a.cap * YLM_HEAD_DIM;
+    const __half *vc = a.v_cache + (size_t)g * a.cap * YLM_HEAD_DIM;
+    struct Chunk
+    {
+        uint4 k[2][4]; // [n-tile][16-byte piece]: token 8 b + hm, dims 32 kq + 8 s ..
+        uint4 v[4][2]; // [token 2 kq + {0, 1, 8, 9}][half]: dims 16 hm ..
+    };
+    auto load_chunk = [&](Chunk &ch, int c) {
+        const int c0 = t0 + 16 * c;
 #pragma unroll
-        for (int u = 0; u < UT; u++)
+        for (int b = 0; b < 2; b++)
         {
-            const int t = t0 + warp + ATC_WARPS * (j0 + u);
-            if (t < te)
-            {
-                kr[u] = __ldg(reinterpret_cast<const uint2 *>(kc + (size_t)t * YLM_HEAD_DIM));
-                vr[u] = __ldg(reinterpret_cast<const uint2 *>(vc + (size_t)t * YLM_HEAD_DIM));
-            }
+            const int t = c0 + 8 * b + hm;
+            const uint4 *src = reinterpret_cast<const uint4 *>(kc + (size_t)t * YLM_HEAD_DIM + 32 * kq);
+#pragma unroll
+            for (int s = 0; s < 4; s++)
+                ch.k[b][s] = t < te ? __ldg(src + s) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+        {
+            const int t = c0 + 2 * kq + (r & 1) + 8 * (r >> 1);
+            const uint4 *src = reinterpret_cast<const uint4 *>(vc + (size_t)t * YLM_HEAD_DIM + 16 * hm);
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+                ch.v[r][hh] = t < te ? __ldg(src + hh) : make_uint4(0, 0, 0, 0);
         }
     };
-    load_batch(0);
+    Chunk bufA, bufB;
+    if (warp < nchunks)
+        load_chunk(bufA, warp);
     pdl_wait();
 
     if (ok)
@@ -432,112 +474,129 @@ __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArg
     }
     __syncthreads();
 
-    float q[G][4], o[G][4], m[G], l[G];
+    // A fragments of Q (FP16 values: prep_head rounds them), rows >= G zero
+    const bool real = hm < G;
+    uint32_t qa[8][2];
 #pragma unroll
-    for (int h = 0; h < G; h++)
+    for (int j = 0; j < 8; j++)
     {
+        const float *qr = q_s + (real ? hm : 0) * YLM_HEAD_DIM + 32 * kq + 8 * (j >> 1) + 4 * (j & 1);
+        const __half2 lo = __floats2half2_rn(qr[0], qr[1]), hi = __floats2half2_rn(qr[2], qr[3]);
+        qa[j][0] = real ? *reinterpret_cast<const uint32_t *>(&lo) : 0u;
+        qa[j][1] = real ? *reinterpret_cast<const uint32_t *>(&hi) : 0u;
+    }
+    float o[16][2];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        o[i][0] = o[i][1] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    auto process = [&](const Chunk &ch, int c) {
+        const int c0 = t0 + 16 * c;
+        float sc[2][2];
+        float z0 = 0.f, z1 = 0.f; // rows 8..15 (A rows zero: stay zero)
+#pragma unroll
+        for (int b = 0; b < 2; b++)
+        {
+            sc[b][0] = sc[b][1] = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+            {
+                const uint4 &w = ch.k[b][j >> 1];
+                const uint32_t b0 = (j & 1) ? w.z : w.x, b1 = (j & 1) ? w.w : w.y;
+                atm_mma(sc[b][0], sc[b][1], z0, z1, qa[j][0], qa[j][1], b0, b1);
+            }
+        }
+        // online softmax of this lane's head over the chunk (base 2); the 4
+        // lanes of a head row hold its 16 scores
+        float s4[4];
 #pragma unroll
         for (int e = 0; e < 4; e++)
         {
-            q[h][e] = q_s[h * YLM_HEAD_DIM + lane * 4 + e] * ATT_SCALE_LOG2;
-            o[h][e] = 0.f;
+            const int t = c0 + 8 * (e >> 1) + 2 * kq + (e & 1);
+            s4[e] = t < te ? sc[e >> 1][e & 1] * ATT_SCALE_LOG2 : -INFINITY;
         }
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-    }
-    const int ntok = max(0, te - t0 - warp);
-    const int per_w = (ntok + ATC_WARPS - 1) / ATC_WARPS; // this warp's cached tokens
-    for (int j0 = 0; j0 < per_w; j0 += UT)
+        float mx = fmaxf(fmaxf(s4[0], s4[1]), fmaxf(s4[2], s4[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m_run, mx);
+        const bool none = mn == -INFINITY || !real;
+        const float cs = none ? 1.f : exp2f(m_run - mn);
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            p[e] = none ? 0.f : exp2f(s4[e] - mn);
+        l_run = l_run * cs + ((p[0] + p[1]) + (p[2] + p[3]));
+        m_run = none ? m_run : mn;
+        const __half2 p01 = __floats2half2_rn(p[0], p[1]), p23 = __floats2half2_rn(p[2], p[3]);
+        const uint32_t pa0 = *reinterpret_cast<const uint32_t *>(&p01);
+        const uint32_t pa2 = *reinterpret_cast<const uint32_t *>(&p23);
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+        {
+            // V of tokens 2 kq + {0, 1} / + {8, 9} at dimension 16 hm + i
+            const uint32_t w0 = reinterpret_cast<const uint32_t *>(&ch.v[0][i >> 3])[(i >> 1) & 3];
+            const uint32_t w1 = reinterpret_cast<const uint32_t *>(&ch.v[1][i >> 3])[(i >> 1) & 3];
+            const uint32_t w2 = reinterpret_cast<const uint32_t *>(&ch.v[2][i >> 3])[(i >> 1) & 3];
+            const uint32_t w3 = reinterpret_cast<const uint32_t *>(&ch.v[3][i >> 3])[(i >> 1) & 3];
+            const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+            o[i][0] *= cs;
+            o[i][1] *= cs;
+            atm_mma(o[i][0], o[i][1], z0, z1, pa0, pa2, __byte_perm(w0, w1, sel), __byte_perm(w2, w3, sel));
+        }
+    };
+    for (int c = warp; c < nchunks; c += 2 * ATC_WARPS)
     {
-        uint2 kcur[UT], vcur[UT];
-#pragma unroll
-        for (int u = 0; u < UT; u++)
-        {
-            kcur[u] = kr[u];
-            vcur[u] = vr[u];
-        }
-        if (j0 + UT < per_w)
-            load_batch(j0 + UT);
-        float sc[UT][G];
-#pragma unroll
-        for (int u = 0; u < UT; u++)
-        {
-            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kcur[u]);
-            const float2 ka = __half22float2(k2[0]), kb = __half22float2(k2[1]);
-#pragma unroll
-            for (int h = 0; h < G; h++)
-                sc[u][h] = fmaf(q[h][3], kb.y, fmaf(q[h][2], kb.x, fmaf(q[h][1], ka.y, q[h][0] * ka.x)));
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-            for (int u = 0; u < UT; u++)
-#pragma unroll
-                for (int h = 0; h < G; h++)
-                    sc[u][h] += __shfl_xor_sync(0xffffffffu, sc[u][h], off);
-#pragma unroll
-        for (int h = 0; h < G; h++)
-        {
-            float mx = m[h];
-#pragma unroll
-            for (int u = 0; u < UT; u++)
-                if (j0 + u < per_w)
-                    mx = fmaxf(mx, sc[u][h]);
-            const float cs = exp2f(m[h] - mx);
-            l[h] *= cs;
-#pragma unroll
-            for (int e = 0; e < 4; e++)
-                o[h][e] *= cs;
-#pragma unroll
-            for (int u = 0; u < UT; u++)
-                if (j0 + u < per_w)
-                {
-                    const float ps = exp2f(sc[u][h] - mx);
-                    const __half2 *v2 = reinterpret_cast<const __half2 *>(&vcur[u]);
-                    const float2 va = __half22float2(v2[0]), vb = __half22float2(v2[1]);
-                    l[h] += ps;
-                    o[h][0] += ps * va.x;
-                    o[h][1] += ps * va.y;
-                    o[h][2] += ps * vb.x;
-                    o[h][3] += ps * vb.y;
-                }
-            m[h] = mx;
-        }
+        if (c + ATC_WARPS < nchunks)
+            load_chunk(bufB, c + ATC_WARPS);
+        process(bufA, c);
+        if (c + ATC_WARPS >= nchunks)
+            break;
+        if (c + 2 * ATC_WARPS < nchunks)
+            load_chunk(bufA, c + 2 * ATC_WARPS);
+        process(bufB, c + ATC_WARPS);
     }
     if (owns_new && warp == 0)
     {
-        // the new token, from shared memory
-#pragma unroll
-        for (int h = 0; h < G; h++)
+        // the new token, from shared memory, in FP32: this lane's quarter of
+        // the score, summed over the head row's 4 lanes
+        float sn = 0.f;
+        if (real)
+#pragma unroll 8
+            for (int d = 0; d < 32; d++)
+                sn = fmaf(q_s[hm * YLM_HEAD_DIM + 32 * kq + d], kn_s[32 * kq + d], sn);
+        sn += __shfl_xor_sync(0xffffffffu, sn, 1);
+        sn += __shfl_xor_sync(0xffffffffu, sn, 2);
+        sn *= ATT_SCALE_LOG2;
+        if (real)
         {
-            float sc = 0.f;
+            const float mn = fmaxf(m_run, sn);
+            const float cs = exp2f(m_run - mn);
+            const float ps = exp2f(sn - mn);
+            l_run = l_run * cs + (kq == 0 ? ps : 0.f);
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                sc = fmaf(q[h][e], kn_s[lane * 4 + e], sc);
-            sc = warp_sum(sc);
-            const float mn = fmaxf(m[h], sc);
-            const float cs = exp2f(m[h] - mn);
-            const float ps = exp2f(sc - mn);
-            l[h] = l[h] * cs + ps;
+            for (int i = 0; i < 16; i++)
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                o[h][e] = o[h][e] * cs + ps * vn_s[lane * 4 + e];
-            m[h] = mn;
+                for (int c = 0; c < 2; c++)
+                    o[i][c] = o[i][c] * cs + ps * vn_s[32 * kq + 16 * c + i];
+            m_run = mn;
         }
     }
     // warp states -> this CTA's partial (M, L, O per head)
-#pragma unroll
-    for (int h = 0; h < G; h++)
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if (real)
     {
-        float *row = mrg + (warp * G + h) * ATT_ROW;
-        if (lane == 0)
+        float *row = mrg + (warp * G + hm) * ATT_ROW;
+        if (kq == 0)
         {
-            row[0] = m[h];
-            row[1] = l[h];
+            row[0] = m_run;
+            row[1] = l_run;
         }
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-            row[2 + lane * 4 + e] = o[h][e];
+        for (int i = 0; i < 16; i++)
+#pragma unroll
+            for (int c = 0; c < 2; c++)
+                row[2 + 32 * kq + 16 * c + i] = o[i][c];
     }
     __syncthreads();
     // this CTA's partial, pushed straight into the cluster: rank q combines
