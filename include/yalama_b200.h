@@ -143,9 +143,14 @@ int ylm_begin_infer(ylm_engine *e);
  * (or every call with the KV cache disabled) is a prefill; later calls take one
  * token. The last-row logits stay on the device (ylm_logits*). */
 int ylm_infer(ylm_engine *e, int64_t *ids, int32_t *n_ids, int32_t *eos_per_prompt, int32_t *n_eos);
-/* Copy the last-row logits to host memory: FP16 (as_float32 = 0) or FP32. */
+/* Copy the last-row logits to host memory: FP16 (as_float32 = 0) or FP32.
+ * Tensor parallel: a greedy decode step (ylm_decode, ylm_generate,
+ * ylm_time_decode) exchanges each rank's best candidate instead of gathering
+ * the logits, so after one this call, ylm_logits_device and ylm_sample first
+ * gather them with one NCCL all-gather: like every engine call with tp_size > 1,
+ * every rank makes it, in the same order. */
 int ylm_logits(ylm_engine *e, void *host_out, int32_t as_float32);
-/* Device pointer of the last-row FP16 logits [vocab]. */
+/* Device pointer of the last-row FP16 logits [vocab] (gathered first, as above). */
 int ylm_logits_device(ylm_engine *e, const void **dev_ptr, int64_t *vocab);
 /* Sampling parameters used by ylm_sample / ylm_decode / ylm_generate. */
 int ylm_set_sampling(ylm_engine *e, const ylm_sampling *s);

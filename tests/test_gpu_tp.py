@@ -70,9 +70,25 @@ def _rank_main(rank, world, port, out_dir):
                 # the advance-mode decode loop (graph replays)
                 assert eng.time_decode(6) > 0
                 loop = eng.logits()
+                # greedy token loops: on the persistent path each rank's best
+                # candidate crosses over peer memory instead of a logits gather,
+                # and the logits are gathered only when read
+                eng.set_sampling(greedy=True)
+                gen = eng.generate(prompt, STEPS)
+                assert gen["status"] == E.Status.OK
+                eng.begin_infer()
+                st, _ = eng.infer(prompt)
+                assert st == E.Status.OK
+                seq = [eng.sample(True)]
+                for _ in range(3):
+                    st, nxt = eng.decode(seq[-1], True)
+                    assert st == E.Status.OK
+                    seq.append(nxt)
+                dec_logits = eng.logits()
                 if rank == 0:
                     np.savez(os.path.join(out_dir, f"{fam}_{persistent}.npz"), rows=np.stack(rows),
-                             toks=np.array(toks), loop=loop)
+                             toks=np.array(toks), loop=loop, gen=gen["ids"], seq=np.array(seq),
+                             dec_logits=dec_logits)
                 eng.close()
                 dist.barrier()
     finally:
@@ -109,6 +125,10 @@ def test_tp_persistent_and_per_op_match_oracle(world, tmp_path):
             np.testing.assert_array_equal(p["toks"], g["toks"])
             np.testing.assert_array_equal(p["loop"], g["loop"])
         for name, r in (("persistent", p), ("per-op", g)):
+            # the greedy loops pick the argmax of the same logits, on every rank
+            np.testing.assert_array_equal(r["gen"], r["toks"])
+            np.testing.assert_array_equal(r["seq"], r["toks"][:4])
+            np.testing.assert_array_equal(r["dec_logits"], r["rows"][3])
             worst = oracle_worst(kw, r["rows"], r["toks"])
             print(f"{fam} tp{world} {name}: max |logit diff| vs oracle = {worst:.3e}")
             assert worst < LOGIT_TOL

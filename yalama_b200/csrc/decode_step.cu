@@ -332,10 +332,72 @@ __device__ __forceinline__ void ds_prologue(const DsArgs &a, const DsPhase &p, i
 __shared__ uint64_t ds_pick[DS_WARPS];
 __shared__ int ds_pick_last;
 
-// (out of line with its three pointers by value: a reference to the kernel
+// One 16-bit payload from a tagged word of this rank's pick mailbox, once the
+// word carries `tag`; bounded as the other waits (after wait_ns, or at once
+// after a recorded error, the current word is used).
+__device__ __forceinline__ uint32_t ds_pick_poll(const uint32_t *w, uint32_t tag, unsigned long long wait_ns, int *err)
+{
+    uint32_t v = __ldcg(w);
+    if ((v & 0xffff0000u) != tag)
+    {
+        const uint64_t t0 = globaltimer_ns();
+        for (int n = 1;; n++)
+        {
+            __nanosleep(64);
+            v = __ldcg(w);
+            if ((v & 0xffff0000u) == tag)
+                break;
+            if ((n & 31) == 0)
+            {
+                if (*reinterpret_cast<volatile int *>(err) != 0)
+                    break;
+                if (globaltimer_ns() - t0 > wait_ns)
+                {
+                    atomicExch(err, YLM_DEV_ERR_TIMEOUT_PEER);
+                    break;
+                }
+            }
+        }
+    }
+    return v & 0xffffu;
+}
+
+// Tensor parallelism: this rank's best key (over its vocabulary rows, global
+// index) to slot `rank` of every rank's pick mailbox as three tagged words
+// (ordered value, index high and low 16 bits; plain stores, over NVLink to the
+// peers), then the maximum over every rank's slot of this rank's own mailbox.
+// Every rank computes the same maximum: the argmax over the whole vocabulary,
+// lowest index among equal values, as the gathered logits' argmax.
+__device__ __forceinline__ uint64_t ds_pick_exchange(uint64_t b, uint32_t *const *pick_mb, int tp, int rank,
+                                                     uint32_t tag, unsigned long long wait_ns, int *err)
+{
+    const uint32_t ord = (uint32_t)(b >> 32) & 0xffffu, idx = key_idx(b);
+    const uint32_t w0 = tag | ord, w1 = tag | (idx >> 16), w2 = tag | (idx & 0xffffu);
+    for (int q = 0; q < tp; q++)
+    {
+        uint32_t *d = pick_mb[q] + 4 * rank;
+        d[0] = w0;
+        d[1] = w1;
+        d[2] = w2;
+    }
+    const uint32_t *mine = pick_mb[rank];
+    uint64_t best = 0;
+    for (int q = 0; q < tp; q++)
+    {
+        const uint32_t o = ds_pick_poll(mine + 4 * q, tag, wait_ns, err);
+        const uint32_t hi = ds_pick_poll(mine + 4 * q + 1, tag, wait_ns, err);
+        const uint32_t lo = ds_pick_poll(mine + 4 * q + 2, tag, wait_ns, err);
+        const uint64_t k = make_key(o, (hi << 16) | lo);
+        best = k > best ? k : best;
+    }
+    return best;
+}
+
+// (out of line with its arguments by value: a reference to the kernel
 // parameters would copy them all to the stack)
 __device__ __noinline__ void ds_greedy_pick(StepState *state, unsigned long long *cand, int *counter, uint64_t best,
-                                            int tid)
+                                            int tid, uint32_t *const *pick_mb, int tp, int rank, uint32_t tag,
+                                            unsigned long long wait_ns, int *err)
 {
     const int warp = tid >> 5, lane = tid & 31;
     best = warp_max_u64(best);
@@ -370,6 +432,8 @@ __device__ __noinline__ void ds_greedy_pick(StepState *state, unsigned long long
         uint64_t b = 0;
         for (int w = 0; w < DS_WARPS; w++)
             b = ds_pick[w] > b ? ds_pick[w] : b;
+        if (tp > 1)
+            b = ds_pick_exchange(b, pick_mb, tp, rank, tag, wait_ns, err);
         StepState *s = state;
         const int64_t id = (int64_t)key_idx(b);
         s->next_token = id;
@@ -456,7 +520,8 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
             p.out[row] = h;
             if (p.greedy_pick)
             {
-                const uint64_t k = make_key(ord16(__half_as_ushort(h)), (uint32_t)row);
+                // the vocabulary index: this rank's rows follow rank * N
+                const uint64_t k = make_key(ord16(__half_as_ushort(h)), (uint32_t)(a.rank * p.N + row));
                 best = k > best ? k : best;
             }
         }
@@ -471,7 +536,8 @@ __device__ __forceinline__ void ds_epilogue(const DsArgs &a, const DsPhase &p, c
         }
     }
     if (p.greedy_pick)
-        ds_greedy_pick(a.pick_state, a.pick_cand, a.pick_counter, best, tid);
+        ds_greedy_pick(a.pick_state, a.pick_cand, a.pick_counter, best, tid, a.pick_mb, a.tp, a.rank, tag, a.wait_ns,
+                       a.err);
 }
 
 // Task cursor of one warp through the phases of a launch: phase, row, chunk,

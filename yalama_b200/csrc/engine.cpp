@@ -309,7 +309,10 @@ struct ylm_engine
     size_t ds_smem = 0;
     int ds_nph = 0;
     std::vector<DsPhase> ds_phases; // the step's GEMV phases (host copy)
-    uint32_t *ds_mb_local[2] = {nullptr, nullptr};  // this rank's two mailbox sets [tp][H]
+    uint32_t *ds_mb_local[2] = {nullptr, nullptr};  // this rank's two mailbox sets [tp][H] (set 0: + [tp][4] pick slots)
+    size_t ds_mb_words[2] = {0, 0};
+    uint32_t **ds_pick_mb = nullptr;                 // device [tp]: every rank's pick slots, mapped here
+    bool logits_partial = false;                     // tensor parallel: only this rank's logits rows are current
     std::vector<void *> ds_mb_peer;                  // peers' mailboxes mapped through CUDA IPC
     uint32_t *ds_xt = nullptr, *ds_actt = nullptr; // tagged residual stream and SwiGLU activations
     unsigned *ds_gen = nullptr;
@@ -381,7 +384,7 @@ struct ylm_engine
                         (void *)partial, (void *)counters, (void *)dstate, (void *)cand, (void *)cand_count,
                         (void *)smp_counter, (void *)dbg_ids, (void *)dbg_probs, (void *)mask_bits, (void *)pX,
                         (void *)pXn, (void *)pQKV, (void *)pQ, (void *)pO, (void *)pA, (void *)pIds, (void *)ds_xt, (void *)ds_actt, (void *)ds_gen, (void *)ds_xstat,
-                        (void *)ds_sink, (void *)pick_cand, (void *)pick_counter})
+                        (void *)ds_sink, (void *)pick_cand, (void *)pick_counter, (void *)ds_pick_mb})
             // logits_local is logits itself without tensor parallelism: free once
             if (p && !(p == (void *)logits_local && logits_local == logits))
                 cudaFree(p);
@@ -857,11 +860,8 @@ struct ylm_engine
             return;
         }
         ds_gen = dalloc<unsigned>(1);
-        if (tp == 1)
-        {
-            pick_cand = dalloc<unsigned long long>(C);
-            pick_counter = dalloc<int>(1);
-        }
+        pick_cand = dalloc<unsigned long long>(C);
+        pick_counter = dalloc<int>(1);
         DsArgs d{};
         d.nph = nph;
         d.tp = tp;
@@ -910,7 +910,8 @@ struct ylm_engine
         cudaIpcMemHandle_t mine[2];
         for (int s = 0; s < 2; s++)
         {
-            ds_mb_local[s] = dalloc<uint32_t>((size_t)tp * H);
+            ds_mb_words[s] = (size_t)tp * H + (s == 0 ? 4 * (size_t)tp : 0);
+            ds_mb_local[s] = dalloc<uint32_t>(ds_mb_words[s]);
             CK(cudaIpcGetMemHandle(&mine[s], ds_mb_local[s]));
         }
         char *dsend = dalloc<char>(sizeof(mine));
@@ -935,6 +936,12 @@ struct ylm_engine
                 ds_mb_peer.push_back(pm);
                 d.mb[s][q] = static_cast<uint32_t *>(pm);
             }
+        // greedy pick slots: after the [tp][H] partials of set 0
+        std::vector<uint32_t *> pm(tp);
+        for (int q = 0; q < tp; q++)
+            pm[q] = d.mb[0][q] + (size_t)tp * H;
+        ds_pick_mb = dalloc<uint32_t *>(tp);
+        h2d(ds_pick_mb, pm.data(), sizeof(uint32_t *) * tp);
     }
 
     // Clear the persistent path's step generation and tagged activations, so no
@@ -946,9 +953,9 @@ struct ylm_engine
         cudaMemsetAsync(ds_actt, 0, sizeof(uint32_t) * inter, st);
         if (pick_counter)
             cudaMemsetAsync(pick_counter, 0, sizeof(int), st);
-        for (uint32_t *m : ds_mb_local)
-            if (m)
-                cudaMemsetAsync(m, 0, sizeof(uint32_t) * tp * H, st);
+        for (int s = 0; s < 2; s++)
+            if (ds_mb_local[s])
+                cudaMemsetAsync(ds_mb_local[s], 0, sizeof(uint32_t) * ds_mb_words[s], st);
     }
 
     // ModelBase::CalculateMaxSequenceLength (ModelBase.cpp:312-338)
@@ -1032,6 +1039,7 @@ struct ylm_engine
                     d.pick_state = dstate;
                     d.pick_cand = pick_cand;
                     d.pick_counter = pick_counter;
+                    d.pick_mb = tp > 1 ? ds_pick_mb : nullptr;
                     CK(ds_launch(d, ds_smem, sms, st));
                     return;
                 }
@@ -1172,6 +1180,9 @@ struct ylm_engine
     {
         xstat_steps++;
         const int mode = step_mode(sample, greedy);
+        // the fused greedy pick exchanges each rank's best candidate instead of
+        // gathering the logits rows: until gather_logits(), each rank holds its own
+        logits_partial = tp > 1 && mode == STEP_GREEDY_FUSED;
         if (ds_on && opt.use_cuda_graph && ds_graph_ok)
         {
             cudaGraphExec_t &ex = graph_for(mode);
@@ -1344,6 +1355,7 @@ struct ylm_engine
         CK(gemv_launch(plm, PRO_RMSNORM, EPI_STORE, f, st, false));
         if (tp > 1)
             NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
+        logits_partial = false;
     }
 
     // -------------------------------------------------------------- Model::Infer
@@ -1427,10 +1439,22 @@ struct ylm_engine
         return YLM_OK;
     }
 
+    // Tensor parallel, after a fused greedy step: the logits rows of every rank
+    // into `logits` (one NCCL all-gather, so every rank makes this call in the
+    // same order, as every other engine call).
+    void gather_logits()
+    {
+        if (!logits_partial)
+            return;
+        NK(ncclAllGather(logits_local, logits, v_local, ncclHalf, comm, st));
+        logits_partial = false;
+    }
+
     int64_t sample(bool do_greedy)
     {
         if (!has_logits)
             fail(YLM_NOT_READY, "no logits to sample");
+        gather_logits();
         fill_state(0, 0, 0, do_greedy, 0);
         push_state();
         CK(sample_launch(sample_args(), st, false));
@@ -1698,6 +1722,7 @@ int ylm_logits(ylm_engine *e, void *host_out, int32_t as_float32)
         if (!e->has_logits)
             fail(YLM_NOT_READY, "no logits yet");
         CK(cudaSetDevice(e->dev));
+        e->gather_logits();
         if (!as_float32)
         {
             CK(cudaMemcpyAsync(host_out, e->logits, e->V * 2, cudaMemcpyDeviceToHost, e->st));
@@ -1716,12 +1741,20 @@ int ylm_logits(ylm_engine *e, void *host_out, int32_t as_float32)
 
 int ylm_logits_device(ylm_engine *e, const void **dev_ptr, int64_t *vocab)
 {
-    if (!e || !dev_ptr)
-        return YLM_INVALID_ARG;
-    *dev_ptr = e->logits;
-    if (vocab)
-        *vocab = e->V;
-    return YLM_OK;
+    return guarded([&]() -> int {
+        if (!e || !dev_ptr)
+            fail(YLM_INVALID_ARG, "null argument");
+        if (e->logits_partial)
+        {
+            CK(cudaSetDevice(e->dev));
+            e->gather_logits();
+            CK(cudaStreamSynchronize(e->st));
+        }
+        *dev_ptr = e->logits;
+        if (vocab)
+            *vocab = e->V;
+        return YLM_OK;
+    });
 }
 
 int ylm_set_sampling(ylm_engine *e, const ylm_sampling *s)

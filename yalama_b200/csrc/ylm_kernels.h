@@ -180,6 +180,10 @@ struct DsArgs
     StepState *pick_state;
     unsigned long long *pick_cand;
     int *pick_counter;
+    // tensor parallelism: pick_mb[q] = rank q's pick mailbox ([tp][4] tagged
+    // words, slot r written by rank r), mapped into this process; a device
+    // array of tp pointers (null without tensor parallelism)
+    uint32_t *const *pick_mb;
     // tensor parallelism: rank `rank` of `tp`; mb[s][q] is mailbox set s + 1 of
     // rank q ([tp][hidden] tagged words, slot r written by rank r), mapped
     // into this process (peer memory over NVLink for q != rank)
