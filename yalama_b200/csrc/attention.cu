@@ -359,6 +359,7 @@ __device__ __forceinline__ void atm_mma(float &d0, float &d1, float &z0, float &
 }
 
 constexpr int ATC_THREADS = 256;
+constexpr int ATC_QF = 20; // words per packed Q-fragment row (16 used)
 constexpr int ATC_WARPS = ATC_THREADS / 32;
 constexpr int ATC_MAX_SPLITS = 16; // largest cluster the kernel supports
 constexpr int ATC_MIN_SPLITS = 8;  // smallest cluster (the portable size)
@@ -369,9 +370,14 @@ static int g_force_split = 0;    // 1: the split-K kernel even where clusters la
 template <int G>
 __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArgs a)
 {
-    __shared__ float q_s[G * YLM_HEAD_DIM];
+    __shared__ __align__(16) float q_s[G * YLM_HEAD_DIM];
     __shared__ float kn_s[YLM_HEAD_DIM], vn_s[YLM_HEAD_DIM];
-    __shared__ float mrg[ATC_WARPS * G * ATT_ROW];
+    __shared__ __align__(16) float mrg[ATC_WARPS * G * ATT_ROW];
+    // Q's A fragments, packed by the warps that prepare the heads: head h,
+    // quarter kq at words [(4 h + kq) * ATC_QF, + 16) (k-step j: words 2 j,
+    // 2 j + 1); the padded stride makes the lanes' 16-byte reads conflict-free.
+    // It lives in mrg until the warp states are written there.
+    uint32_t *qfrag = reinterpret_cast<uint32_t *>(mrg);
     __shared__ float recv[ATC_MAX_SPLITS * G * (2 + YLM_HEAD_DIM / ATC_MIN_SPLITS)]; // [rank][head][M, L, slice]
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
@@ -454,8 +460,17 @@ __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArg
         for (int h = warp; h < G + 2; h += ATC_WARPS)
         {
             if (h < G)
+            {
                 prep_head(a.qkv + (size_t)(g * G + h) * YLM_HEAD_DIM, a.q_norm, a.eps, cosr, sinr, true,
                           q_s + h * YLM_HEAD_DIM, lane);
+                __syncwarp();
+                // lane l holds dimensions 4 l .. 4 l + 3 = quarter l / 8, k-step
+                // l % 8 (32 kq + 8 s + 4 t = 4 l); FP16 values (prep_head rounds)
+                const float4 v = *reinterpret_cast<const float4 *>(q_s + h * YLM_HEAD_DIM + 4 * lane);
+                const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+                *reinterpret_cast<uint2 *>(qfrag + (4 * h + (lane >> 3)) * ATC_QF + 2 * (lane & 7)) =
+                    make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+            }
             else if (h == G && owns_new)
             {
                 prep_head(a.qkv + (size_t)(a.hq + g) * YLM_HEAD_DIM, a.k_norm, a.eps, cosr, sinr, true, kn_s, lane);
@@ -474,17 +489,27 @@ __global__ void __launch_bounds__(ATC_THREADS) attn_cluster_kernel(const AttnArg
     }
     __syncthreads();
 
-    // A fragments of Q (FP16 values: prep_head rounds them), rows >= G zero
+    // A fragments of Q, rows >= G zero (only warps with chunks use them)
     const bool real = hm < G;
     uint32_t qa[8][2];
-#pragma unroll
-    for (int j = 0; j < 8; j++)
+    if (real && warp < nchunks)
     {
-        const float *qr = q_s + (real ? hm : 0) * YLM_HEAD_DIM + 32 * kq + 8 * (j >> 1) + 4 * (j & 1);
-        const __half2 lo = __floats2half2_rn(qr[0], qr[1]), hi = __floats2half2_rn(qr[2], qr[3]);
-        qa[j][0] = real ? *reinterpret_cast<const uint32_t *>(&lo) : 0u;
-        qa[j][1] = real ? *reinterpret_cast<const uint32_t *>(&hi) : 0u;
+        const uint4 *f = reinterpret_cast<const uint4 *>(qfrag + (4 * hm + kq) * ATC_QF);
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+        {
+            const uint4 w = f[r];
+            qa[2 * r][0] = w.x;
+            qa[2 * r][1] = w.y;
+            qa[2 * r + 1][0] = w.z;
+            qa[2 * r + 1][1] = w.w;
+        }
     }
+    else
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            qa[j][0] = qa[j][1] = 0u;
+    __syncthreads(); // qfrag is read before any warp writes its state into mrg
     float o[16][2];
 #pragma unroll
     for (int i = 0; i < 16; i++)
