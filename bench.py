@@ -513,11 +513,12 @@ def bench_ours(a):
             pg.barrier()
         return
     # decode launches per token: persistent path = one GEMV segment per layer
-    # plus one, attention per layer, sampler; per-op graph = QKV, attention,
+    # plus one, attention per layer, and a sampler launch only for top-k (a
+    # greedy pick runs in the lm_head epilogue); per-op graph = QKV, attention,
     # O, gate-up, down per layer (+ residual adds with tensor parallelism),
     # lm_head, sampler; NCCL's all-reduce / all-gather kernels are not counted
     if r["persistent"]:
-        launches_per_token = 2 * spec.layers + 2
+        launches_per_token = 2 * spec.layers + 1 + (1 if a.top_k else 0)
     else:
         launches_per_token = spec.layers * (5 if world == 1 else 7) + 2
     n_dec = a.decode - 1
