@@ -41,14 +41,16 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# name -> (model preset, prompt tokens, generated tokens, top_k (0 = greedy), temperature)
+# name -> (model preset, prompt tokens, generated tokens, top_k (0 = greedy), temperature,
+#          KV cache GB: the reference's --kvcachesizeingb; its capacity rule (EnsureKVCapacity,
+#          src/models/ModelBase.cpp:853-866) needs 3 GB for a 4096 + 512 request at 70B)
 WORKLOADS = {
-    "llama3.1-8b": ("llama3.1-8b", 2048, 1024, 0, 0.6),
-    "llama3.2-3b": ("llama3.2-3b", 512, 256, 40, 0.6),
-    "qwen3-0.6b": ("qwen3-0.6b", 32, 128, 0, 0.6),
-    "qwen2.5-7b": ("qwen2.5-7b", 8192, 512, 0, 0.6),
-    "mistral-7b-v0.3": ("mistral-7b-v0.3", 2048, 1024, 0, 0.6),
-    "llama3.1-70b": ("llama3.1-70b", 4096, 512, 0, 0.6),
+    "llama3.1-8b": ("llama3.1-8b", 2048, 1024, 0, 0.6, 2),
+    "llama3.2-3b": ("llama3.2-3b", 512, 256, 40, 0.6, 2),
+    "qwen3-0.6b": ("qwen3-0.6b", 32, 128, 0, 0.6, 2),
+    "qwen2.5-7b": ("qwen2.5-7b", 8192, 512, 0, 0.6, 2),
+    "mistral-7b-v0.3": ("mistral-7b-v0.3", 2048, 1024, 0, 0.6, 2),
+    "llama3.1-70b": ("llama3.1-70b", 4096, 512, 0, 0.6, 3),
 }
 DEFAULT_WORKLOAD = "llama3.1-8b"
 EXTRA_WORKLOAD = "llama3.2-3b"
@@ -148,8 +150,9 @@ def args_():
     ap.add_argument("--decode-path", default="persistent", choices=["persistent", "per-op"],
                     help="persistent GEMV segments (default) or the per-op graph")
     a = ap.parse_args()
-    preset, prompt, decode, top_k, temp = WORKLOADS[a.workload]
+    preset, prompt, decode, top_k, temp, kv_gb = WORKLOADS[a.workload]
     a.preset = preset
+    a.kv_gb = kv_gb
     a.prompt = a.prompt or prompt
     a.decode = a.decode or decode
     a.top_k, a.temperature = top_k, temp
@@ -295,7 +298,8 @@ def bench_reference(a):
 
 def workload_desc(a, spec):
     return (f"{a.preset}-shaped FP16{f' ({a.layers} layers)' if a.layers else ''}, batch 1, prompt {a.prompt}, "
-            f"{a.decode} generated tokens, {sampling_desc(a.top_k, a.temperature)}")
+            f"{a.decode} generated tokens, {sampling_desc(a.top_k, a.temperature)}"
+            f"{f', KV cache {a.kv_gb} GB' if a.kv_gb != 2 else ''}")
 
 
 def gpu_reference(spec, prompt, top_k, temp):
@@ -398,7 +402,8 @@ def run_workload(a, rank, world, local, pg, nccl_id, spec, steps, warmup, e2e_re
 
     cfg = E.config_from_spec(spec)
     eng = E.Engine(None, cfg, nccl_id=nccl_id, device=local, tp_rank=rank, tp_size=world,
-                   init_seed=SEEDS["weight_seed"], decode_persistent=int(a.decode_path == "persistent"))
+                   init_seed=SEEDS["weight_seed"], decode_persistent=int(a.decode_path == "persistent"),
+                   kv_cache_gb=a.kv_gb)
     greedy = a.top_k == 0
     eng.set_sampling(greedy=greedy, top_k=a.top_k or 40, temperature=a.temperature, seed=SEEDS["sample_seed"])
     prompt = synth.prompt_ids(SEEDS["prompt_seed"], a.prompt, spec.vocab)
@@ -499,7 +504,7 @@ def bench_ours(a):
     extra = None
     if world == 1 and not a.no_extra and not a.layers and a.workload != EXTRA_WORKLOAD:
         b = argparse.Namespace(**vars(a))
-        b.preset, b.prompt, b.decode, b.top_k, b.temperature = WORKLOADS[EXTRA_WORKLOAD]
+        b.preset, b.prompt, b.decode, b.top_k, b.temperature, b.kv_gb = WORKLOADS[EXTRA_WORKLOAD]
         espec = synth.PRESETS[b.preset]
         er = run_workload(b, rank, world, local, pg, nccl_id, espec, 2, 1, 1, False)
         ebpt = decode_bytes_per_token(espec, b.prompt + b.decode // 2, 1)
