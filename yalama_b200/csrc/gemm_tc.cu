@@ -469,7 +469,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     float *xsum = xrow + 256;                                                          // sums [2][128]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int qb = blockIdx.x, h = blockIdx.y, g = h / (p.hq / p.hkv);
+    // heaviest query tiles first: linear block i (the order blocks start in)
+    // takes tile nq - 1 - i / hq of head i % hq, so the causal tiles with the
+    // most key tiles fill the first waves and the short ones the last
+    const int lin = blockIdx.y * gridDim.x + blockIdx.x;
+    const int qb = (int)gridDim.x - 1 - lin / p.hq, h = lin % p.hq, g = h / (p.hq / p.hkv);
     const int r0 = qb * FT_BM;
     const int nt = qb + 1; // key tiles 0 .. the diagonal one
 
