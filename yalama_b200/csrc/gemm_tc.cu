@@ -64,6 +64,17 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, 
                  : "memory");
 }
 
+// The same with A read from tensor memory (lane = row of A, its K elements
+// packed two FP16 per 32-bit column).
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+                 "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t *bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -547,7 +558,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             const uint32_t idesc_s = tc_idesc(FT_BM, FT_BN);
             const uint32_t idesc_o = tc_idesc(FT_BM, 128) | (1u << 16); // B (V) MN-major
             bool ok = mbar_wait_bounded(q_full, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
-            const uint32_t q0 = smem_u32(sq), pb = smem_u32(sp);
+            const uint32_t q0 = smem_u32(sq);
             // S_j = Q K_j^T into TMEM columns [128 (j & 1), +128)
             auto issue_s = [&](int j) {
                 const int s = j & 1;
@@ -583,13 +594,13 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t v0 = smem_u32(sv + s * FT_TILE);
+                // O += P V with P (FP16, packed by the softmax warps over the
+                // first 64 columns of this tile's S buffer) as A from TMEM:
+                // keys 16 kk .. 16 kk + 15 are columns 8 kk .. 8 kk + 7
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++)
-                {
-                    const uint32_t poff = (uint32_t)((kk >> 2) * (FT_TILE / 2) + (kk & 3) * 32);
-                    tc_mma(tmem + 256, smem_desc_k128(pb + poff), smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024),
-                           idesc_o, (j | kk) ? 1u : 0u);
-                }
+                    tc_mma_ts(tmem + 256, tmem + 128u * (uint32_t)s + 8u * (uint32_t)kk,
+                              smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024), idesc_o, (j | kk) ? 1u : 0u);
                 tc_commit(o_full);
                 tc_commit(&kv_empty[s]);
             }
@@ -663,13 +674,15 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 break;
             }
             mx = fmaxf(mx, xrow[(hf ^ 1) * 128 + row]);
-            // each tile holds key j*128 <= every row of this block: mx is finite
-            const float mn = fmaxf(m, mx);
-            const float corr = exp2f(m - mn);
-            m = mn;
-            // the previous P V has finished (P and the O columns are free):
-            // rescale this row of O unless no row of the warp changed its maximum
-            if (j > 0)
+            // each tile holds key j*128 <= every row of this block: mx is finite.
+            // The exponent base m moves only when the row maximum rises by more
+            // than 8 (base 2): P = exp2(s - m) <= 2^8 stays exact in FP16 range,
+            // O and l carry the same factor, and O is rescaled (waiting for the
+            // previous P V) only on such a rise, not on every new maximum.
+            float corr = 1.f;
+            if (j == 0)
+                m = mx;
+            else if (__any_sync(0xffffffffu, mx > m + 8.f))
             {
                 if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_full, (j - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL)))
                 {
@@ -677,49 +690,43 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                if (!__all_sync(0xffffffffu, corr == 1.f))
+                if (mx > m + 8.f)
                 {
-#pragma unroll
-                    for (int c0 = cb; c0 < cb + 64; c0 += 32)
-                    {
-                        float v[32];
-                        tmem_ld32(trow + 256u + (uint32_t)c0, v);
-#pragma unroll
-                        for (int i = 0; i < 32; i++)
-                            v[i] *= corr;
-                        tmem_st32(trow + 256u + (uint32_t)c0, v);
-                    }
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    corr = exp2f(m - mx);
+                    m = mx;
                 }
+#pragma unroll
+                for (int c0 = cb; c0 < cb + 64; c0 += 32)
+                {
+                    float v[32];
+                    tmem_ld32(trow + 256u + (uint32_t)c0, v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        v[i] *= corr;
+                    tmem_st32(trow + 256u + (uint32_t)c0, v);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
-            // pass 2: P = exp2(s - m) in FP16, 16-byte chunks into the swizzled layout
+            const float mn = m;
+            // pass 2: P = exp2(s - m) in FP16, packed two per column into this
+            // tile's S buffer, columns [32 hf, 32 hf + 32) (this thread's keys;
+            // both halves have read their scores by now: xbar)
             // (masked keys hold -inf: exp2 gives 0)
             float sum = 0.f;
+            uint32_t pk[32];
 #pragma unroll
-            for (int c0 = 0; c0 < 64; c0 += 32)
+            for (int i = 0; i < 64; i += 2)
             {
-                uint32_t pk[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2)
-                {
-                    const float p0 = ex2_ftz(v[c0 + i] - mn);
-                    const float p1 = ex2_ftz(v[c0 + i + 1] - mn);
-                    sum += p0 + p1;
-                    const __half2 hp = __floats2half2_rn(p0, p1);
-                    pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&hp);
-                }
-#pragma unroll
-                for (int ch = 0; ch < 4; ch++)
-                {
-                    const int c = ((cb + c0) >> 3) + ch; // 16-byte chunk of the row: keys 8c .. 8c + 7
-                    uint8_t *dst = sp + (c >> 3) * (FT_TILE / 2) + row * 128 + (((c & 7) ^ (row & 7)) << 4);
-                    *reinterpret_cast<uint4 *>(dst) =
-                        make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-                }
+                const float p0 = ex2_ftz(v[i] - mn);
+                const float p1 = ex2_ftz(v[i + 1] - mn);
+                sum += p0 + p1;
+                const __half2 hp = __floats2half2_rn(p0, p1);
+                pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&hp);
             }
+            tmem_st32(tS + 32u * (uint32_t)hf, reinterpret_cast<const float *>(pk));
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             l = l * corr + sum;
-            // P visible to the tensor cores; this thread's TMEM reads and writes done
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            // P visible to the tensor cores
             tc_fence_before();
             mbar_arrive(p_full);
         }
@@ -732,7 +739,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             fw = mbar_wait_bounded(xbar, nt & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL);
             l += xsum[(hf ^ 1) * 128 + row];
         }
-        fw = fw && mbar_wait_bounded(o_full, (nt - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
+        // every MMA of the CTA has completed (`done`, committed once after the
+        // last P V: its single phase cannot alias, while o_full may be one or
+        // two phases behind this warp's last wait on it)
+        fw = fw && mbar_wait_bounded(done, 0, p.err, YLM_DEV_ERR_TIMEOUT_FULL) && !*abort_flag;
         if (__all_sync(0xffffffffu, fw))
         {
             tc_fence_after();
