@@ -149,6 +149,8 @@ def args_():
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--decode-path", default="persistent", choices=["persistent", "per-op"],
                     help="persistent GEMV segments (default) or the per-op graph")
+    ap.add_argument("--kernels", action="store_true",
+                    help="time the prefill kernels alone (tcgen05 GEMM beside cuBLAS, causal attention) and exit")
     a = ap.parse_args()
     preset, prompt, decode, top_k, temp, kv_gb = WORKLOADS[a.workload]
     a.preset = preset
@@ -575,8 +577,68 @@ def bench_ours(a):
         pg.barrier()
 
 
+# ---------------------------------------------------------------- prefill kernels alone
+GEMM_SHAPES = [(2048, 6144, 4096), (2048, 4096, 4096), (2048, 28672, 4096), (2048, 4096, 14336), (8192, 4608, 3584),
+               (512, 16384, 3072)]
+ATTN_SHAPES = [(2048, 32, 8), (8192, 28, 4), (512, 24, 8)]
+
+
+def bench_kernels():
+    """The prefill kernels through their C-ABI entry points on random FP16
+    inputs, CUDA events on the launching stream, after 3 warm-up launches: the
+    tcgen05 GEMM (ylm_k_gemm) at the Llama-3.1-8B, Qwen2.5-7B and Llama-3.2-3B
+    projection shapes beside cuBLAS (torch.matmul, the same FP16 operands), and
+    the causal attention (ylm_k_prefill_attention, tcgen05 and mma.sync). Order
+    of attention launches: per shape 3 + 10 tcgen05, then 3 + 10 mma.sync."""
+    import torch
+    from yalama_b200 import engine as E
+    L = E.lib()
+    st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    out = {"attention": [], "gemm": []}
+    for T, hq, hkv in ATTN_SHAPES:
+        q = torch.randn(T, hq * 128, device="cuda", dtype=torch.float16)
+        kc = torch.randn(hkv, T, 128, device="cuda", dtype=torch.float16)
+        vc = torch.randn(hkv, T, 128, device="cuda", dtype=torch.float16)
+        o = torch.empty(T, hq * 128, device="cuda", dtype=torch.float16)
+        flops = 4 * hq * 128 * T * T / 2
+        row = {"T": T, "hq": hq, "hkv": hkv}
+        for name, tc in (("tcgen05", 1), ("mma_sync", 0)):
+            ms = timed(lambda: E.check(L.ylm_k_prefill_attention(ptr(q), ptr(kc), ptr(vc), T, hq, hkv, T, ptr(o), tc,
+                                                                 st()), "attention"), 10)
+            row[name + "_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+        out["attention"].append(row)
+    for T, N, K in GEMM_SHAPES:
+        a = torch.randn(T, K, device="cuda", dtype=torch.float16) * 0.1
+        w = torch.randn(N, K, device="cuda", dtype=torch.float16) * 0.1
+        c = torch.empty(T, N, device="cuda", dtype=torch.float16)
+        t_own = timed(lambda: E.check(L.ylm_k_gemm(ptr(a), ptr(w), T, N, K, ptr(c), 1, st()), "gemm"), 20)
+        t_lib = timed(lambda: torch.matmul(a, w.t()), 20)
+        f = 2 * T * N * K
+        out["gemm"].append({"T": T, "N": N, "K": K, "tcgen05_tflops": round(f / (t_own * 1e-3) / 1e12, 1),
+                            "cublas_tflops": round(f / (t_lib * 1e-3) / 1e12, 1)})
+    print(json.dumps({"kernels": out, "unit": "TFLOP/s (FP16 in, FP32 accumulate)",
+                      "timing": "CUDA events, 3 warm-up launches, mean of 10 (attention) / 20 (GEMM)"}), flush=True)
+
+
 def main():
     a = args_()
+    if a.kernels:
+        bench_kernels()
+        return
     if a.impl == "reference":
         bench_reference(a)
     else:
