@@ -408,24 +408,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // prefill SDPA of ModelBase.cpp:671-693 with the causal mask of :620-636
 // (implicit) and no ExpandKV (:695-707): query head h reads KV head h / G from
 // the cache. One CTA per 128 query rows of one head, 10 warps:
-//   warp 0      TMA: the Q tile once, then K and V tiles of 128 keys (two
-//               stages) from 3-D tensor maps whose key extent is the prompt
-//               length, so keys past it arrive as zeros
+//   warp 0      TMA: the Q tile once, then K tiles of 128 keys (three
+//               stages, two tiles ahead) and V tiles (two stages) from 3-D
+//               tensor maps whose key extent is the prompt length, so keys
+//               past it arrive as zeros
 //   warp 1      one thread issues S = Q K^T (M=128, N=128, K=128, both K-major)
 //               into TMEM columns [0, 128), then O += P V into [128, 256)
-//               (P K-major from shared memory, V MN-major: the tile as stored)
+//               (P from TMEM, V MN-major: the tile as stored)
 //   warps 2-9   one query row per two threads (their TMEM lane; 64 of the
 //               row's columns each, maxima and sums exchanged through shared
 //               memory): scale, causal mask,
-//               running max, P = exp2(s - m) rounded to FP16 into shared memory
-//               in the 128-byte-swizzled K-major layout; O accumulates in TMEM
-//               across tiles and is rescaled in place (tcgen05.ld / st) before
-//               the next P V whenever a row's maximum grew
+//               running max, P = exp2(s - m) rounded to FP16 and packed into
+//               the tile's TMEM score buffer; O accumulates in TMEM across
+//               tiles and is rescaled in place (tcgen05.ld / st) before the
+//               next P V when a row's maximum rose by more than 2^8
 // All waits are bounded; a timeout records YLM_DEV_ERR_TIMEOUT_* and unwinds.
 constexpr int FT_BM = 128, FT_BN = 128, FT_THREADS = 320; // TMA, MMA, 8 softmax warps
 constexpr int FT_TILE = 128 * 128 * 2; // one 128 x 128 FP16 tile: two 64-column atoms of 16 KB
 constexpr int FT_TMEM_COLS = 512; // S for two key tiles (double-buffered), then O
-constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * 6 + 256 + 2 * 2 * 128 * 4; // Q, K x2, V x2, P, barriers, row exchange
+constexpr int FT_KST = 3, FT_VST = 2;  // K and V stages
+constexpr size_t FT_SMEM = 1024 + (size_t)FT_TILE * (1 + FT_KST + FT_VST) + 256 + 2 * 2 * 128 * 4; // Q, K, V, barriers, row exchange
 
 // MN-major operand tile with the 128-byte swizzle: 64-element rows along MN,
 // `lbo` bytes between 64-element MN blocks, `sbo` bytes between 8-row K groups.
@@ -467,15 +469,18 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *sq = smem;
-    uint8_t *sk = sq + FT_TILE;         // 2 stages
-    uint8_t *sv = sk + 2 * FT_TILE;     // 2 stages
-    uint8_t *sp = sv + 2 * FT_TILE;     // P
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sp + FT_TILE);
-    uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 7,
-             *o_full = bars + 8, *done = bars + 9;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 10);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 11);
-    uint64_t *xbar = bars + 12; // row exchange between the two softmax halves (256 arrivals)
+    uint8_t *sk = sq + FT_TILE;           // FT_KST stages
+    uint8_t *sv = sk + FT_KST * FT_TILE;  // FT_VST stages
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sv + FT_VST * FT_TILE);
+    // K and V have rings of their own: a K stage is free once its S = Q K^T
+    // completes, a V stage once its P V does, so the next tiles' keys load
+    // while the current P V waits for its softmax
+    uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = k_full + FT_KST, *v_full = k_empty + FT_KST,
+             *v_empty = v_full + FT_VST, *s_full = v_empty + FT_VST, *p_full = s_full + 2, *o_full = p_full + 1,
+             *done = o_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(done + 2);
+    uint64_t *xbar = done + 3; // row exchange between the two softmax halves (256 arrivals)
     float *xrow = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256); // maxima [2 halves][128 rows]
     float *xsum = xrow + 256;                                                          // sums [2][128]
 
@@ -491,10 +496,15 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     if (threadIdx.x == 0)
     {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; s++)
+        for (int s = 0; s < FT_KST; s++)
         {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < FT_VST; s++)
+        {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         mbar_init(&s_full[0], 1);
         mbar_init(&s_full[1], 1);
@@ -527,28 +537,49 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             mbar_arrive_expect_tx(q_full, FT_TILE);
             tma_load_2d(sq, &qmap, h * 128, r0, q_full);
             tma_load_2d(sq + FT_TILE / 2, &qmap, h * 128 + 64, r0, q_full);
-            int issued = 0;
-            for (int j = 0; j < nt; j++)
+            // K tile j into stage j % FT_KST once S of tile j - FT_KST is done;
+            // V tile j into stage j % FT_VST once P V of tile j - FT_VST is
+            // done; the keys run FT_KST - 1 tiles ahead of the values
+            int kissued = 0, vissued = 0;
+            auto load_k = [&](int j) {
+                const int s = j % FT_KST;
+                if (j >= FT_KST &&
+                    !mbar_wait_bounded(&k_empty[s], (j / FT_KST - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                    return false;
+                mbar_arrive_expect_tx(&k_full[s], FT_TILE);
+                tma_load_3d(sk + s * FT_TILE, &kmap, 0, j * FT_BN, g, &k_full[s]);
+                tma_load_3d(sk + s * FT_TILE + FT_TILE / 2, &kmap, 64, j * FT_BN, g, &k_full[s]);
+                kissued++;
+                return true;
+            };
+            auto load_v = [&](int j) {
+                const int s = j % FT_VST;
+                if (j >= FT_VST &&
+                    !mbar_wait_bounded(&v_empty[s], (j / FT_VST - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                    return false;
+                mbar_arrive_expect_tx(&v_full[s], FT_TILE);
+                tma_load_3d(sv + s * FT_TILE, &vmap, 0, j * FT_BN, g, &v_full[s]);
+                tma_load_3d(sv + s * FT_TILE + FT_TILE / 2, &vmap, 64, j * FT_BN, g, &v_full[s]);
+                vissued++;
+                return true;
+            };
+            constexpr int AHEAD = FT_KST - 1;
+            for (int j = 0; j < nt + AHEAD; j++)
             {
-                const int s = j & 1;
-                if (j >= 2 && !mbar_wait_bounded(&kv_empty[s], ((j >> 1) - 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_EMPTY))
+                if (*abort_flag)
+                    break;
+                if ((j < nt && !load_k(j)) || (j >= AHEAD && !load_v(j - AHEAD)))
                 {
                     *abort_flag = 1;
                     break;
                 }
-                if (*abort_flag)
-                    break;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * FT_TILE);
-                tma_load_3d(sk + s * FT_TILE, &kmap, 0, j * FT_BN, g, &kv_full[s]);
-                tma_load_3d(sk + s * FT_TILE + FT_TILE / 2, &kmap, 64, j * FT_BN, g, &kv_full[s]);
-                tma_load_3d(sv + s * FT_TILE, &vmap, 0, j * FT_BN, g, &kv_full[s]);
-                tma_load_3d(sv + s * FT_TILE + FT_TILE / 2, &vmap, 64, j * FT_BN, g, &kv_full[s]);
-                issued++;
             }
             // every issued copy has landed before the CTA can exit
             mbar_wait_bounded(q_full, 0, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
-            for (int j = issued > 2 ? issued - 2 : 0; j < issued; j++)
-                mbar_wait_bounded(&kv_full[j & 1], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+            for (int j = kissued > FT_KST ? kissued - FT_KST : 0; j < kissued; j++)
+                mbar_wait_bounded(&k_full[j % FT_KST], (j / FT_KST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
+            for (int j = vissued > FT_VST ? vissued - FT_VST : 0; j < vissued; j++)
+                mbar_wait_bounded(&v_full[j % FT_VST], (j / FT_VST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_DRAIN);
         }
     }
     else if (warp == 1)
@@ -561,11 +592,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             const uint32_t q0 = smem_u32(sq);
             // S_j = Q K_j^T into TMEM columns [128 (j & 1), +128)
             auto issue_s = [&](int j) {
-                const int s = j & 1;
-                if (!mbar_wait_bounded(&kv_full[s], (j >> 1) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                const int s = j & 1, ks = j % FT_KST;
+                if (!mbar_wait_bounded(&k_full[ks], (j / FT_KST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
                     return false;
                 tc_fence_after();
-                const uint32_t k0 = smem_u32(sk + s * FT_TILE);
+                const uint32_t k0 = smem_u32(sk + ks * FT_TILE);
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++)
                 {
@@ -573,6 +604,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     tc_mma(tmem + 128u * s, smem_desc_k128(q0 + off), smem_desc_k128(k0 + off), idesc_s, kk ? 1u : 0u);
                 }
                 tc_commit(&s_full[s]);
+                tc_commit(&k_empty[ks]);
                 return true;
             };
             ok = ok && issue_s(0);
@@ -587,13 +619,15 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     ok = false;
                     break;
                 }
-                if (!mbar_wait_bounded(p_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
+                const int vs = j % FT_VST;
+                if (!mbar_wait_bounded(p_full, j & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL) ||
+                    !mbar_wait_bounded(&v_full[vs], (j / FT_VST) & 1, p.err, YLM_DEV_ERR_TIMEOUT_FULL))
                 {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t v0 = smem_u32(sv + s * FT_TILE);
+                const uint32_t v0 = smem_u32(sv + vs * FT_TILE);
                 // O += P V with P (FP16, packed by the softmax warps over the
                 // first 64 columns of this tile's S buffer) as A from TMEM:
                 // keys 16 kk .. 16 kk + 15 are columns 8 kk .. 8 kk + 7
@@ -602,7 +636,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     tc_mma_ts(tmem + 256, tmem + 128u * (uint32_t)s + 8u * (uint32_t)kk,
                               smem_desc_mn128(v0 + kk * 2048, FT_TILE / 2, 1024), idesc_o, (j | kk) ? 1u : 0u);
                 tc_commit(o_full);
-                tc_commit(&kv_empty[s]);
+                tc_commit(&v_empty[vs]);
             }
             if (!ok)
                 *abort_flag = 1;
