@@ -121,6 +121,27 @@ __device__ __forceinline__ void hist_add(int *hist, uint32_t bin, bool valid)
         atomicAdd(&hist[bin], __popc(peers));
 }
 
+// The bin of the k-th largest value in sh.hist, counting `above` values
+// already known to lie above every bin: the highest bin b with
+// above + count(bins > b) < k <= above + count(bins >= b), or bin 0 when the
+// bins hold fewer than k (then count(bins > 0)). Thread t looks at bin 255 - t
+// so one block-wide exclusive scan gives every bin's count above it.
+// Writes sh.sel[out] = b, sh.sel[out + 1] = above + count(bins > b).
+__device__ __forceinline__ void threshold_bin(int k, int above, SelectShared &sh, int out)
+{
+    static_assert(SMP_THREADS == 256, "one thread per bin");
+    const int b = 255 - (int)threadIdx.x;
+    const int hv = sh.hist[b];
+    int tot;
+    const int excl = above + block_excl_scan(hv, sh.wsum, &tot);
+    if (excl < k && (excl + hv >= k || b == 0))
+    {
+        sh.sel[out] = b;
+        sh.sel[out + 1] = excl;
+    }
+    __syncthreads();
+}
+
 // Threshold T (16-bit ordered value) such that fewer than k values exceed T and
 // at least k are >= T; also returns how many exceed it. `val(e)` gives the
 // ordered value of element e of this thread, e < n_mine; every thread loops to
@@ -139,19 +160,7 @@ __device__ __forceinline__ void radix_threshold(int k, int n_mine, int n_max, Va
         hist_add(sh.hist, ok ? (val(e) >> 8) : 0u, ok);
     }
     __syncthreads();
-    if (tid == 0)
-    {
-        int cum = 0, b = 255;
-        for (; b > 0; b--)
-        {
-            if (cum + sh.hist[b] >= k)
-                break;
-            cum += sh.hist[b];
-        }
-        sh.sel[0] = b;
-        sh.sel[1] = cum;
-    }
-    __syncthreads();
+    threshold_bin(k, 0, sh, 0);
     const uint32_t B1 = (uint32_t)sh.sel[0];
     const int gt1 = sh.sel[1];
     for (int b = tid; b < 256; b += SMP_THREADS)
@@ -164,19 +173,7 @@ __device__ __forceinline__ void radix_threshold(int k, int n_mine, int n_max, Va
         hist_add(sh.hist, v & 255, ok && (v >> 8) == B1);
     }
     __syncthreads();
-    if (tid == 0)
-    {
-        int cum = gt1, b = 255;
-        for (; b > 0; b--)
-        {
-            if (cum + sh.hist[b] >= k)
-                break;
-            cum += sh.hist[b];
-        }
-        sh.sel[2] = b;
-        sh.sel[3] = cum;
-    }
-    __syncthreads();
+    threshold_bin(k, gt1, sh, 2);
     *T_out = (B1 << 8) | (uint32_t)sh.sel[2];
     *gt_out = sh.sel[3];
     __syncthreads();
