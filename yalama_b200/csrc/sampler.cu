@@ -489,10 +489,14 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const SampleArgs a)
     }
 }
 
+// As few parts as the per-thread register budget allows (SMP_E elements a
+// thread): the last CTA merges parts x K candidates, so fewer, fuller parts
+// shorten the serial end of the kernel (63 parts at a 128k vocabulary: top-k
+// step overhead 30.8 -> 24.8 us at the Llama-3.2-3B shape against 126).
 int sample_parts(int64_t vocab, int num_sms)
 {
-    int64_t p = std::min<int64_t>(num_sms, (vocab + 1023) / 1024);
-    p = std::max<int64_t>(p, (vocab + SMP_THREADS * SMP_E - 1) / (SMP_THREADS * SMP_E));
+    (void)num_sms;
+    const int64_t p = (vocab + SMP_THREADS * SMP_E - 1) / (SMP_THREADS * SMP_E);
     return (int)std::max<int64_t>(1, p);
 }
 
