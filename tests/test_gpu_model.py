@@ -31,11 +31,11 @@ FAMILIES = {
 }
 
 
-def make(kw, seed=0, snapshot=None, tmp=None, **opts):
+def make(kw, seed=0, snapshot=None, tmp=None, through_bf16=False, **opts):
     spec = synth.tiny_spec(**kw)
     snap = None
     if snapshot:
-        snap = synth.write_snapshot(str(tmp), spec, seed=seed, dtype=snapshot)
+        snap = synth.write_snapshot(str(tmp), spec, seed=seed, dtype=snapshot, through_bf16=through_bf16)
     eng = E.Engine(snap, E.config_from_spec(spec), init_seed=seed, **opts)
     return spec, eng
 
@@ -93,20 +93,29 @@ def test_split_attention_kernel_logits_match_oracle(fam):
 
 
 def test_snapshot_load_equals_random_init(tmp_path):
+    """The loader (pinned row bands, BF16 / F32 converted on the device) gives
+    the weights bit for bit: F16 and F32 shards of the generator's values load
+    as the random init does, and BF16 shards load as an F16 snapshot of the
+    same values rounded to BF16 (qwen2: QKV biases, untied lm_head)."""
     kw = FAMILIES["qwen2"]
     spec, a = make(kw)
     _, b = make(kw, snapshot="F16", tmp=tmp_path / "f16")
     _, c = make(kw, snapshot="BF16", tmp=tmp_path / "bf16")
+    _, d = make(kw, snapshot="F32", tmp=tmp_path / "f32")
+    _, e = make(kw, snapshot="F16", tmp=tmp_path / "f16_of_bf16", through_bf16=True)
     prompt = synth.prompt_ids(1, 16, spec.vocab)
     outs = []
-    for eng in (a, b, c):
+    for eng in (a, b, c, d, e):
         eng.begin_infer()
         st, _ = eng.infer(prompt)
         assert st == E.Status.OK
         outs.append(eng.logits())
     # the same FP16 weights through the counter-based generator and through the loader
     np.testing.assert_array_equal(outs[0], outs[1])
-    # BF16 shards hold the same values rounded to BF16: close, not equal
+    np.testing.assert_array_equal(outs[0], outs[3])
+    # BF16 shards decode to exactly the BF16-rounded values
+    np.testing.assert_array_equal(outs[2], outs[4])
+    # and those differ from the FP16 weights by BF16 rounding only: close, not equal
     assert np.max(np.abs(outs[0] - outs[2])) < 5e-2
 
 

@@ -33,6 +33,7 @@
 #include <mutex>
 #include <sstream>
 #include <stdexcept>
+#include <thread>
 #include <string>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -620,11 +621,49 @@ struct ylm_engine
         }
     }
 
+    // Row bands of every piece move through a ring of pinned host buffers:
+    // host threads copy band k out of the mapped shard (the page faults of a
+    // cold file are spread over them) while the engine stream copies earlier
+    // bands to the device; BF16 / F32 bands land in a device staging buffer
+    // and are converted to FP16 there (round to nearest even, as on the host).
+    // Each piece's slice is read straight from the mapping: a rank's rows or
+    // columns only (tensor parallelism).
     void load_weights(const char *dir)
     {
         Snapshot snap;
         snap.open_dir(dir);
-        std::vector<__half> stage;
+        constexpr int NB = 3;
+        constexpr size_t CH = (size_t)64 << 20;
+        struct Ring
+        {
+            void *host[NB] = {}, *dev[NB] = {};
+            cudaEvent_t ev[NB] = {};
+            bool used[NB] = {};
+            ~Ring()
+            {
+                for (int k = 0; k < NB; k++)
+                {
+                    if (ev[k])
+                    {
+                        cudaEventSynchronize(ev[k]);
+                        cudaEventDestroy(ev[k]);
+                    }
+                    if (host[k])
+                        cudaFreeHost(host[k]);
+                    if (dev[k])
+                        cudaFree(dev[k]);
+                }
+            }
+        } ring;
+        for (int k = 0; k < NB; k++)
+        {
+            CK(cudaHostAlloc(&ring.host[k], CH, cudaHostAllocDefault));
+            CK(cudaMalloc(&ring.dev[k], CH));
+            CK(cudaEventCreateWithFlags(&ring.ev[k], cudaEventDisableTiming));
+        }
+        const unsigned hc = std::thread::hardware_concurrency();
+        const int nthreads = (int)std::max(1u, std::min(8u, hc ? hc : 1u));
+        int k = 0;
         for (auto &p : pieces())
         {
             const StTensor *t = snap.find(p.name);
@@ -644,38 +683,50 @@ struct ylm_engine
                 fail(YLM_LOAD_ERROR, "tensor %s: rank %zu", p.name.c_str(), t->shape.size());
             if (p.r0 + p.nr > rows || p.c0 + p.nc > cols || (size_t)(rows * cols) * es != t->bytes)
                 fail(YLM_LOAD_ERROR, "tensor %s: shape does not match the model config", p.name.c_str());
+            const size_t row_bytes = (size_t)p.nc * es, src_stride = (size_t)cols * es;
+            if (row_bytes > CH)
+                fail(YLM_LOAD_ERROR, "tensor %s: rows wider than the staging buffer", p.name.c_str());
             const uint8_t *src = t->data + ((size_t)p.r0 * cols + p.c0) * es;
-            if (dc == 0)
-            {
-                CK(cudaMemcpy2DAsync(p.dst, p.ld * 2, src, cols * 2, p.nc * 2, p.nr, cudaMemcpyHostToDevice, st));
-                CK(cudaStreamSynchronize(st));
-                continue;
-            }
-            // BF16 / F32 shards: convert on the host, one row band at a time
-            const int64_t band = std::max<int64_t>(1, (64 << 20) / (p.nc * 2));
+            const int64_t band = std::min<int64_t>(65535, std::max<int64_t>(1, (int64_t)(CH / row_bytes)));
             for (int64_t r = 0; r < p.nr; r += band)
             {
                 const int64_t nr = std::min(band, p.nr - r);
-                stage.resize((size_t)nr * p.nc);
-                for (int64_t i = 0; i < nr; i++)
-                    for (int64_t j = 0; j < p.nc; j++)
-                    {
-                        const uint8_t *e = src + ((size_t)(r + i) * cols + j) * es;
-                        float f;
-                        if (dc == 1)
-                        {
-                            uint32_t u = (uint32_t)(e[0] | (e[1] << 8)) << 16;
-                            memcpy(&f, &u, 4);
-                        }
-                        else
-                            memcpy(&f, e, 4);
-                        stage[(size_t)i * p.nc + j] = __float2half_rn(f);
-                    }
-                CK(cudaMemcpy2DAsync(p.dst + (size_t)r * p.ld, p.ld * 2, stage.data(), p.nc * 2, p.nc * 2, nr,
-                                     cudaMemcpyHostToDevice, st));
-                CK(cudaStreamSynchronize(st)); // `stage` is refilled next
+                if (ring.used[k])
+                    CK(cudaEventSynchronize(ring.ev[k]));
+                uint8_t *hb = static_cast<uint8_t *>(ring.host[k]);
+                const uint8_t *s0 = src + (size_t)r * src_stride;
+                auto copy_rows = [&](int64_t a, int64_t b) {
+                    if (row_bytes == src_stride)
+                        memcpy(hb + (size_t)a * row_bytes, s0 + (size_t)a * src_stride, (size_t)(b - a) * row_bytes);
+                    else
+                        for (int64_t i = a; i < b; i++)
+                            memcpy(hb + (size_t)i * row_bytes, s0 + (size_t)i * src_stride, row_bytes);
+                };
+                const int nt = (int)std::min<int64_t>(nthreads, std::max<int64_t>(1, (int64_t)(nr * row_bytes >> 22)));
+                if (nt <= 1)
+                    copy_rows(0, nr);
+                else
+                {
+                    std::vector<std::thread> th;
+                    for (int q = 0; q < nt; q++)
+                        th.emplace_back(copy_rows, nr * q / nt, nr * (q + 1) / nt);
+                    for (auto &x : th)
+                        x.join();
+                }
+                if (dc == 0)
+                    CK(cudaMemcpy2DAsync(p.dst + (size_t)r * p.ld, p.ld * 2, hb, row_bytes, row_bytes, nr,
+                                         cudaMemcpyHostToDevice, st));
+                else
+                {
+                    CK(cudaMemcpyAsync(ring.dev[k], hb, (size_t)nr * row_bytes, cudaMemcpyHostToDevice, st));
+                    CK(convert_rows_launch(ring.dev[k], dc, nr, p.nc, p.dst + (size_t)r * p.ld, p.ld, st));
+                }
+                CK(cudaEventRecord(ring.ev[k], st));
+                ring.used[k] = true;
+                k = (k + 1) % NB;
             }
         }
+        CK(cudaStreamSynchronize(st));
     }
 
     void build_plans()

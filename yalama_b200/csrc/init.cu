@@ -65,23 +65,31 @@ cudaError_t fill_const_launch(__half *dst, int64_t n, float v, cudaStream_t s)
     return cudaGetLastError();
 }
 
-// src_dtype: 1 = BF16, 2 = F32 (F16 is copied as is by the caller)
-__global__ void convert_kernel(const void *src, int src_dtype, __half *dst, int64_t n)
+// A dense band [nr][nc] of BF16 (src_dtype 1) or F32 (2) values -> FP16 rows
+// of `dst` with row stride `ld`, rounded to nearest even (as __float2half_rn
+// on the host). Grid: x over column blocks, y over rows (nr <= 65535).
+__global__ void convert_rows_kernel(const void *src, int src_dtype, int64_t nc, __half *dst, int64_t ld)
 {
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x)
+    const int64_t r = blockIdx.y;
+    __half *d = dst + r * ld;
+    for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < nc; c += (int64_t)gridDim.x * blockDim.x)
     {
-        float f = src_dtype == 1 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(src)[t])
-                                 : reinterpret_cast<const float *>(src)[t];
-        dst[t] = __float2half_rn(f);
+        const int64_t t = r * nc + c;
+        const float f = src_dtype == 1 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(src)[t])
+                                       : reinterpret_cast<const float *>(src)[t];
+        d[c] = __float2half_rn(f);
     }
 }
 
-cudaError_t convert_to_half_launch(const void *src, int src_dtype, __half *dst, int64_t n, cudaStream_t s)
+cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t nr, int64_t nc, __half *dst, int64_t ld,
+                                cudaStream_t s)
 {
-    if (n <= 0)
+    if (nr <= 0 || nc <= 0)
         return cudaSuccess;
-    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 32);
-    convert_kernel<<<blocks, 256, 0, s>>>(src, src_dtype, dst, n);
+    if (nr > 65535 || (src_dtype != 1 && src_dtype != 2))
+        return cudaErrorInvalidValue;
+    const unsigned bx = (unsigned)std::min<int64_t>((nc + 255) / 256, 16);
+    convert_rows_kernel<<<dim3(bx, (unsigned)nr), 256, 0, s>>>(src, src_dtype, nc, dst, ld);
     return cudaGetLastError();
 }
 

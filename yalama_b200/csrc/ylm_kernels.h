@@ -263,6 +263,8 @@ cudaError_t attn_prefill_launch(const __half *q, const __half *k_cache, const __
 cudaError_t fill_normal_launch(__half *dst, int64_t rows, int64_t cols, int64_t ld, uint64_t key, int64_t row0,
                                int64_t col0, int64_t full_cols, double stdv, cudaStream_t s);
 cudaError_t fill_const_launch(__half *dst, int64_t n, float v, cudaStream_t s);
-cudaError_t convert_to_half_launch(const void *src, int src_dtype, __half *dst, int64_t n, cudaStream_t s);
+// Dense [nr][nc] BF16 (1) / F32 (2) -> FP16 rows of dst (stride ld), nr <= 65535.
+cudaError_t convert_rows_launch(const void *src, int src_dtype, int64_t nr, int64_t nc, __half *dst, int64_t ld,
+                                cudaStream_t s);
 
 } // namespace ylm

@@ -283,10 +283,21 @@ def tiled_values(block: np.ndarray, start: int, shape: Tuple[int, ...]) -> np.nd
     return out.reshape(shape)
 
 
+def round_bf16(a: np.ndarray) -> np.ndarray:
+    """float32 values rounded to BF16 (nearest even), as float32."""
+    f = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    r = ((f + np.uint32(0x7FFF) + ((f >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)) << np.uint32(16)
+    return r.view(np.float32)
+
+
 def write_snapshot(root: str, spec: ModelSpec, seed: int = 0, dtype: str = "F16",
                    std: float = 0.02, shard_bytes: int = 4 << 30, fast: bool = False,
-                   snapshot_hash: str = "0000000000000000000000000000000000000000") -> str:
+                   snapshot_hash: str = "0000000000000000000000000000000000000000",
+                   through_bf16: bool = False) -> str:
     """Write an HF hub layout under `root`; return the snapshot directory.
+
+    `through_bf16=True` rounds every value to BF16 before it is stored as
+    `dtype` (an F16 snapshot then holds exactly what a BF16 one decodes to).
 
     `fast=True` fills the weights from one block of ``TILE_PERIOD`` N(0, std)
     values (numpy PCG64 from the seed), each tensor reading the block
@@ -314,8 +325,10 @@ def write_snapshot(root: str, spec: ModelSpec, seed: int = 0, dtype: str = "F16"
     def producer(name, shape):
         def make():
             if fast and not name.endswith("norm.weight"):
-                return tiled_values(block, fnv1a64(name) % TILE_PERIOD, shape)
-            return tensor_values(seed, name, shape, std)
+                v = tiled_values(block, fnv1a64(name) % TILE_PERIOD, shape)
+            else:
+                v = tensor_values(seed, name, shape, std)
+            return round_bf16(v).reshape(v.shape) if through_bf16 else v
         return make
 
     shards: List[List] = [[]]
