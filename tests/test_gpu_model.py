@@ -17,7 +17,7 @@ from oracle.numerics import sampler_uniform
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-# north_star: logits within max-abs 2e-2 of the reference FP16 path
+# the parity bar: logits within max-abs 2e-2 of the reference FP16 path
 LOGIT_TOL = 2e-2
 # greedy ids may differ only where the top-2 logit gap is below this
 TIE_GAP = 1e-2

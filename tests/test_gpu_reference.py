@@ -38,7 +38,7 @@ pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_GPU_F16 = os.path.join(ROOT, "oracle", "_ref", "ref_gpu_f16")
-# north_star: logits within max-abs 2e-2 (FP16) of the reference's FP16 path
+# the parity bar: logits within max-abs 2e-2 (FP16) of the reference's FP16 path
 LOGIT_TOL = 2e-2
 # greedy ids may differ only where the reference's top-2 logit gap is below this
 TIE_GAP = 1e-2
