@@ -71,6 +71,38 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peaks():
+    """Dense 16-bit tensor-core rate (TF/s): burst and sustained, measured with
+    a cuBLAS bf16 GEMM on this kind of GPU (FP16 runs at the same dense rate)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if d.get("bf16_tflops"):
+            burst = float(d["bf16_tflops"])
+            return burst, float(d.get("bf16_tflops_sustained") or burst), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def prefill_flops(spec, T):
+    """Algorithmic FLOPs of one T-token prefill as the engine computes it: the
+    four projections on every row, causal attention (QK^T and PV over keys
+    0..i for query i) and the lm_head on the last row only."""
+    H, D, I, V = spec.hidden, spec.head_dim, spec.intermediate, spec.vocab
+    proj = H * (spec.heads + 2 * spec.kv_heads) * D + spec.heads * D * H + 3 * H * I
+    attn = 4 * D * spec.heads * T * (T + 1) // 2
+    return spec.layers * (2 * T * proj + attn) + 2 * V * H
+
+
+def prefill_roofline(spec, T, tok_s, tp):
+    burst, sustained, kind = tensor_peaks()
+    fl = prefill_flops(spec, T) / tp
+    achieved = fl * tok_s / T / 1e12
+    return {"flops_per_prefill_per_gpu": fl, "achieved_tflops": achieved, "peak_tflops": burst,
+            "frac": achieved / burst, "frac_of_sustained": achieved / sustained, "peak_kind": kind,
+            "note": "FP16 tensor-core FLOPs (projections on all rows, causal attention, last-row lm_head) "
+                    "over CUDA-event prefill time, against the cuBLAS bf16 burst rate (sustained beside it)"}
+
+
 def profile_traffic(name):
     """traffic (bytes per launch) recorded from an ncu capture under profiles/."""
     p = os.path.join(ROOT, "profiles", name)
@@ -513,6 +545,7 @@ def bench_ours(a):
         extra = {"workload": workload_desc(b, espec), "value": er["value"], "unit": "tok/s",
                  "ms_per_token": er["ms_per_token"], "prefill_tok_s": er["prefill_tok_s"],
                  "decode_roofline_frac": ebpt / (er["ms_per_token"] * 1e-3) / 1e9 / hbm,
+                 "prefill_roofline_frac": prefill_roofline(espec, b.prompt, er["prefill_tok_s"], 1)["frac"],
                  "e2e": er["e2e"], "steps": 2, "warmup": 1}
 
     if rank != 0:
@@ -542,7 +575,9 @@ def bench_ours(a):
                        "decode_path": "persistent GEMV segments" if r["persistent"] else "per-op graph",
                        "l2": f"weights {bpt * world / 1e9:.1f} GB >> 126 MB L2 (no flush needed)",
                        "timing": "CUDA events on the engine stream; value = decode tokens / decode time"},
-            "prefill_tok_s": r["prefill_tok_s"], "decode_roofline": step_roof, "roofline": r.get("roofline"),
+            "prefill_tok_s": r["prefill_tok_s"],
+            "prefill_roofline": prefill_roofline(spec, a.prompt, r["prefill_tok_s"], world),
+            "decode_roofline": step_roof, "roofline": r.get("roofline"),
             "e2e": {"value": r["e2e"], "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "ylm_generate (C ABI), host prompt in, host ids out, per-token sync"},
             "gpu_launches": gpu_launches, "wall_s_timed": r["wall"], "clocks": r["clocks"]}
