@@ -783,10 +783,11 @@ void attn_force_split_kernel(bool on) { g_force_split = on ? 1 : 0; }
 bool attn_uses_split_kernel() { return g_force_split || g_cluster_splits == 0; }
 
 // Cluster size for a launch over `hkv` KV heads: 8 CTAs per head with 8 or
-// more heads (the Llama-3.1-8B shape on one GPU measured 3.23 ms per decode
-// step with 8-CTA clusters against 3.37 with 16; Qwen3-0.6B 0.80 against 0.82),
-// 16 with fewer heads (a tensor-parallel rank's share), so the launch still
-// spreads over more SMs.
+// more heads (the Llama-3.1-8B shape on one GPU, 2048-token prompt, measured
+// 3.03 ms per decode step with 8-CTA clusters against 3.19 with 16 and 3.12
+// with 4; Qwen3-0.6B, 32-token prompt, 0.83 ms against 0.94 and 0.82: fewer
+// CTAs only pay at short contexts), 16 with fewer heads (a tensor-parallel
+// rank's share), so the launch still spreads over more SMs.
 static int attn_cluster_size(int hkv)
 {
     if (g_force_split || g_cluster_splits == 0)
