@@ -126,3 +126,47 @@ def test_create_rejects_bad_shapes():
     with pytest.raises(E.YlmError) as ei:
         E.Engine(None, c)
     assert ei.value.status == E.Status.UNSUPPORTED
+
+
+def test_engine_calls_reject_a_null_engine():
+    # every engine-level call checks its handle before any device work, so a
+    # NULL engine is INVALID_ARG (ylm_destroy(NULL) is a no-op, like free)
+    L = E.lib()
+    inv = E.Status.INVALID_ARG
+    assert L.ylm_destroy(None) == E.Status.OK
+    assert L.ylm_begin_infer(None) == inv
+    assert L.ylm_infer(None, None, None, None, None) == inv
+    assert L.ylm_logits(None, None, 0) == inv
+    assert L.ylm_logits_device(None, None, None) == inv
+    assert L.ylm_set_sampling(None, None) == inv
+    assert L.ylm_sample(None, 1, None) == inv
+    assert L.ylm_decode(None, 0, 1, None) == inv
+    assert L.ylm_generate(None, None, 0, 0, None, 0, None, None, None, None) == inv
+    assert L.ylm_set_draw(None, 0.5) == inv
+    assert L.ylm_last_topk(None, None, None, None, None) == inv
+    assert L.ylm_info(None, None, None, None) == inv
+    assert L.ylm_last_prefill_ms(None, None) == inv
+    assert L.ylm_decode_path(None, None) == inv
+    assert L.ylm_time_decode(None, 1, None) == inv
+    assert L.ylm_time_segment(None, 0, 1, None, None) == inv
+    assert L.ylm_exchange_stats(None, 0, None, None, None) == inv
+    assert L.ylm_time_allreduce(None, 1, None) == inv
+    assert L.ylm_debug_drop_output(None, 0) == inv
+    assert L.ylm_options_default(None) == inv
+    assert L.ylm_config_from_json(None, None) == inv
+    assert L.ylm_resolve_snapshot(None, None, 0) == inv
+
+
+def test_more_kernel_entry_points_validate_arguments():
+    L = E.lib()
+    inv = E.Status.INVALID_ARG
+    assert L.ylm_k_prefill_attention(None, None, None, 16, 4, 2, 8, None, 1, None) == inv
+    # grouped-query shapes the kernels do not cover: hq not a multiple of hkv,
+    # more than 8 query heads per KV head
+    p = ctypes.c_void_p(256)
+    assert L.ylm_k_decode_attention(p, None, None, 1e-6, p, p, 16, p, p, 8, 6, 4, 0, 0, p, None) == inv
+    assert L.ylm_k_decode_attention(p, None, None, 1e-6, p, p, 16, p, p, 8, 18, 2, 0, 0, p, None) == inv
+    # slot past the cache, RoPE position past the table
+    assert L.ylm_k_decode_attention(p, None, None, 1e-6, p, p, 16, p, p, 8, 4, 2, 8, 0, p, None) == inv
+    assert L.ylm_k_decode_attention(p, None, None, 1e-6, p, p, 16, p, p, 8, 4, 2, 0, 16, p, None) == inv
+    assert L.ylm_k_decode_attention_noalloc(p, None, None, 1e-6, p, p, 16, p, p, 8, 4, 2, 8, 0, p, None) == inv
